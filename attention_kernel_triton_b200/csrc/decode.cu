@@ -1,0 +1,770 @@
+// Split-KV GQA decode for sm_100a: dense ("redundant") and paged var-len.
+//
+// Replaces the Triton kernels of decode_flash_attention_redundant.py:71-229
+// and decode_flash_attention_redundant_var_len_paged.py:70-224.  Same math
+// (one query row per qo head, softmax over every valid key, fp32
+// accumulation; the reference's online-softmax recurrence is at DR:44-62 /
+// DP:45-63), different machine mapping:
+//
+//  * GQA packing: one CTA owns (sequence, kv head, group of G qo heads,
+//    chunk of tokens) and reads each K/V byte of its chunk once for all G
+//    heads (the reference runs one program per qo head and re-reads K/V G
+//    times, DP:124-127).
+//  * Split-KV: a sequence's tokens are cut into chunks of C tokens; each chunk
+//    is one CTA writing a partial (O normalised, log2-sum-exp) that the merge
+//    kernel combines.  The reference scans a whole sequence in one program
+//    (DP:168), with no LSE output.
+//  * Staging: warp 0 is a producer that resolves page ids through the page
+//    table and moves K and V tiles HBM->shared with 1-D bulk copies on the
+//    TMA engine (cp.async.bulk + mbarrier complete_tx) into a ring of stages;
+//    warps 1..4 consume tiles round-robin.  A tile never straddles a page.
+//  * CUDA cores only (decode is HBM-bound): q.k with packed fp32x2 FMAs,
+//    an 8-lane reduce-scatter that leaves each lane the score of one
+//    (token, head), exp2 with the scale folded into q, P.V with fp32x2 FMAs.
+#include "common.cuh"
+#include "profile.cuh"
+
+#include <algorithm>
+#include <cstdio>
+#include <cstring>
+#include <string>
+
+namespace akt {
+
+__device__ unsigned int g_device_status = 0;
+
+constexpr int kProducerWarps = 1;
+constexpr int kConsumerWarps = 4;
+constexpr int kDecodeThreads = 32 * (kProducerWarps + kConsumerWarps);
+constexpr int kSubTile = 16;  // tokens per online-softmax step of a consumer warp
+
+struct DecodeParams {
+  const void* q;
+  int64_t q_sb, q_sh;  // q element strides (dim stride must be 1)
+  // K/V addressing.  Dense: base of K / V, strides (batch, head, token).
+  // Paged: k = pool, v = pool + stride_kv, strides (page, head, token).
+  const void* k;
+  const void* v;
+  int64_t s0, s_head, s_tok;
+  const int32_t* indptr;
+  const int32_t* indices;
+  const int32_t* last_len;
+  int64_t num_pages;
+  int64_t num_page_entries;
+  void* out;
+  int64_t o_sb, o_sh, o_sd;
+  int B, Hq, Hkv;
+  int L;  // dense sequence length
+  int P;  // page size
+  int group;          // Hq / Hkv
+  int g_tiles;        // group / G_TILE
+  int units;          // Hkv * g_tiles
+  int tile_tokens;    // tokens per stage (divides P when paged)
+  int chunk_tokens;   // multiple of tile_tokens
+  int chunks_per_seq; // dense only
+  int num_stages;
+  float scale_log2;   // softmax_scale * log2(e)
+  float* part_o;      // [items, G_TILE, D]
+  float* part_lse;    // [items, G_TILE]   (log2 domain)
+  int* chunk_offset;  // [B + 1] paged only
+  int direct_out;     // every unit has one chunk: write O directly
+};
+
+// ---------------------------------------------------------------------------
+// planner: per-sequence chunk counts -> exclusive prefix (one CTA)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ int paged_seq_len(const DecodeParams& p, int b) {
+  int s = p.indptr[b], e = p.indptr[b + 1];
+  int np = e - s;
+  if (np <= 0) return 0;
+  int last = p.last_len[b];
+  last = last < 0 ? 0 : (last > p.P ? p.P : last);
+  return (np - 1) * p.P + last;
+}
+
+__global__ void __launch_bounds__(1024) paged_plan_kernel(DecodeParams p) {
+  __shared__ int warp_sums[32];
+  __shared__ int carry;
+  if (threadIdx.x == 0) carry = 0;
+  __syncthreads();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int base = 0; base < p.B; base += 1024) {
+    int b = base + threadIdx.x;
+    int n = 0;
+    if (b < p.B) {
+      int s = p.indptr[b], e = p.indptr[b + 1];
+      if (e < s || s < 0 || e > p.num_page_entries) {
+        record_status(kStatusBadIndptr);
+      } else {
+        n = cdiv(paged_seq_len(p, b), p.chunk_tokens);
+      }
+    }
+    int x = n;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      int y = __shfl_up_sync(0xffffffffu, x, o);
+      if (lane >= o) x += y;
+    }
+    if (lane == 31) warp_sums[warp] = x;
+    __syncthreads();
+    if (warp == 0) {
+      int w = warp_sums[lane];
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        int y = __shfl_up_sync(0xffffffffu, w, o);
+        if (lane >= o) w += y;
+      }
+      warp_sums[lane] = w;
+    }
+    __syncthreads();
+    const int incl = x + (warp > 0 ? warp_sums[warp - 1] : 0);  // inclusive, within this block
+    if (b < p.B) p.chunk_offset[b] = carry + incl - n;
+    __syncthreads();
+    if (threadIdx.x == 1023) carry += incl;  // n == 0 past the end, so this is the block total
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) p.chunk_offset[p.B] = carry;
+}
+
+// ---------------------------------------------------------------------------
+// main split-KV kernel
+// ---------------------------------------------------------------------------
+template <typename T, int D, int G, bool PAGED>
+__global__ void __launch_bounds__(kDecodeThreads, (G * D > 512) ? 2 : 3) decode_splitkv_kernel(const DecodeParams p) {
+  static_assert(D % 64 == 0 && D <= 256, "head_dim");
+  static_assert(G == 1 || G == 2 || G == 4 || G == 8, "group tile");
+  constexpr int CH = D / 64;      // 16-byte chunks per lane per token row (8 lanes per row)
+  constexpr int DPL = D / 32;     // output dims per lane in P.V
+  constexpr int LPH = 8 / G;      // lanes sharing one (token, head) score after reduce-scatter
+  using E = Elem<T>;
+
+  extern __shared__ __align__(128) unsigned char smem[];
+  const int NS = p.num_stages;
+  const int TT = p.tile_tokens;
+  const int stage_elems = TT * D;
+  T* kv_s = reinterpret_cast<T*>(smem);  // [NS][2][TT][D]
+  float* comb = reinterpret_cast<float*>(smem + (size_t)NS * 2 * stage_elems * sizeof(T));
+  float* comb_m = comb;                               // [NW][G]
+  float* comb_l = comb_m + kConsumerWarps * G;        // [NW][G]
+  float* comb_o = comb_l + kConsumerWarps * G;        // [NW][G][D]
+  float* p_s = comb_o + kConsumerWarps * G * D;       // [NW][kSubTile][G]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(p_s + kConsumerWarps * kSubTile * G);
+  uint64_t* full = bars;        // [NS]
+  uint64_t* empty = bars + NS;  // [NS]
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  // ---- work item -> (sequence, unit, token range)
+  const int item = blockIdx.x;
+  const int cg = item / p.units;
+  const int unit = item - cg * p.units;
+  int b, c, seq_len;
+  if (PAGED) {
+    const int total = p.chunk_offset[p.B];
+    if (cg >= total) return;
+    int lo = 0, hi = p.B - 1;  // largest b with chunk_offset[b] <= cg
+    while (lo < hi) {
+      int mid = (lo + hi + 1) >> 1;
+      if (p.chunk_offset[mid] <= cg) lo = mid; else hi = mid - 1;
+    }
+    b = lo;
+    c = cg - p.chunk_offset[b];
+    seq_len = paged_seq_len(p, b);
+  } else {
+    b = cg / p.chunks_per_seq;
+    c = cg - b * p.chunks_per_seq;
+    seq_len = p.L;
+  }
+  const int tok_begin = c * p.chunk_tokens;
+  const int tok_end = min(seq_len, tok_begin + p.chunk_tokens);
+  const int n_tiles = cdiv(tok_end - tok_begin, TT);
+  const int kvh = unit / p.g_tiles;
+  const int head0 = kvh * p.group + (unit - kvh * p.g_tiles) * G;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  if (warp < kProducerWarps) {
+    // ======================= producer =======================
+    const uint64_t pol = l2_policy_evict_first();
+    const uint32_t row_bytes = D * sizeof(T);
+    const T* kbase = static_cast<const T*>(p.k);
+    const T* vbase = static_cast<const T*>(p.v);
+    int page_base = 0, npages = 0, batch_lo = -1, my_pid = -1, issued = 0;
+    if (PAGED) {
+      page_base = p.indptr[b];
+      npages = p.indptr[b + 1] - page_base;
+    }
+    for (int t = 0; t < n_tiles; ++t) {
+      const int slot = t % NS;
+      const uint32_t phase = (uint32_t)(t / NS) & 1u;
+      const int tok = tok_begin + t * TT;
+      const int n = min(TT, tok_end - tok);
+      int64_t off;
+      bool ok_addr = true;
+      if (PAGED) {
+        const int pl = tok / p.P;
+        if (batch_lo < 0 || pl >= batch_lo + 32) {
+          batch_lo = pl;
+          const int j = batch_lo + lane;
+          my_pid = (j < npages) ? __ldg(p.indices + page_base + j) : -1;
+        }
+        const int pid = __shfl_sync(0xffffffffu, my_pid, pl - batch_lo);
+        if (pid < 0 || (int64_t)pid >= p.num_pages) {
+          ok_addr = false;
+          off = 0;
+        } else {
+          off = (int64_t)pid * p.s0 + (int64_t)kvh * p.s_head + (int64_t)(tok - pl * p.P) * p.s_tok;
+        }
+      } else {
+        off = (int64_t)b * p.s0 + (int64_t)kvh * p.s_head + (int64_t)tok * p.s_tok;
+      }
+      bool ok = true;
+      if (t >= NS && lane == 0) ok = mbar_wait(&empty[slot], phase ^ 1u);
+      if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) break;
+      issued = t + 1;
+      if (lane == 0) {
+        T* dst = kv_s + (size_t)slot * 2 * stage_elems;
+        if (ok_addr) {
+          const uint32_t bytes = (uint32_t)n * row_bytes;
+          mbar_arrive_expect_tx(&full[slot], 2u * bytes);
+          bulk_g2s(dst, kbase + off, bytes, &full[slot], pol);
+          bulk_g2s(dst + stage_elems, vbase + off, bytes, &full[slot], pol);
+        } else {
+          record_status(kStatusBadPage);
+          mbar_arrive(&full[slot]);
+        }
+      }
+      __syncwarp();
+    }
+    // Do not exit while bulk copies into this CTA's shared memory are in
+    // flight: wait (bounded) for the full barrier of every issued tile that
+    // no consumer has waited on yet (consumers wait on all of them on the
+    // normal path, so this returns at once there).
+    if (lane == 0) {
+      for (int t = max(0, issued - NS); t < issued; ++t) mbar_wait(&full[t % NS], (uint32_t)(t / NS) & 1u);
+    }
+    return;
+  }
+
+  // ========================= consumers =========================
+  const int cw = warp - kProducerWarps;
+  const int tg = lane >> 3;  // token group within a pass (4 tokens per pass)
+  const int li = lane & 7;   // lane within the 8-lane row group
+  const int my_head = li / LPH;
+
+  // q for the G heads, scaled by softmax_scale*log2(e); lane li holds 16-byte
+  // chunks li, li+8, ... of each row
+  float2 qf[G][CH][4];
+  {
+    const T* qb = static_cast<const T*>(p.q) + (int64_t)b * p.q_sb;
+#pragma unroll
+    for (int h = 0; h < G; ++h) {
+      const T* qh = qb + (int64_t)(head0 + h) * p.q_sh;
+#pragma unroll
+      for (int cc = 0; cc < CH; ++cc) {
+        const uint4 raw = *reinterpret_cast<const uint4*>(qh + (li + 8 * cc) * 8);
+        const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          float2 f = E::to_float2(w[j]);
+          qf[h][cc][j] = make_float2(f.x * p.scale_log2, f.y * p.scale_log2);
+        }
+      }
+    }
+  }
+
+  float m_own = -INFINITY;  // running max (log2 units) of head my_head
+  float l_own = 0.f;        // partial sum of p over this lane's tokens, head my_head
+  float2 o[G][DPL / 2];
+#pragma unroll
+  for (int h = 0; h < G; ++h)
+#pragma unroll
+    for (int j = 0; j < DPL / 2; ++j) o[h][j] = make_float2(0.f, 0.f);
+
+  float* pw = p_s + cw * kSubTile * G;
+  bool alive = true;
+
+  for (int t = cw; t < n_tiles && alive; t += kConsumerWarps) {
+    const int slot = t % NS;
+    const uint32_t phase = (uint32_t)(t / NS) & 1u;
+    if (!mbar_wait(&full[slot], phase)) { alive = false; break; }
+    const int n = min(TT, tok_end - (tok_begin + t * TT));
+    const T* Ks = kv_s + (size_t)slot * 2 * stage_elems;
+    const T* Vs = Ks + stage_elems;
+
+    for (int sub = 0; sub < n; sub += kSubTile) {
+      float sc[kSubTile / 4];
+#pragma unroll
+      for (int pass = 0; pass < kSubTile / 4; ++pass) {
+        const int row = sub + pass * 4 + tg;
+        const int rr = row < TT ? row : TT - 1;  // stay inside the stage
+        float2 acc[G];
+#pragma unroll
+        for (int h = 0; h < G; ++h) acc[h] = make_float2(0.f, 0.f);
+#pragma unroll
+        for (int cc = 0; cc < CH; ++cc) {
+          const uint4 raw = *reinterpret_cast<const uint4*>(Ks + rr * D + (li + 8 * cc) * 8);
+          const float2 k0 = E::to_float2(raw.x), k1 = E::to_float2(raw.y);
+          const float2 k2 = E::to_float2(raw.z), k3 = E::to_float2(raw.w);
+#pragma unroll
+          for (int h = 0; h < G; ++h) {
+            acc[h] = ffma2(qf[h][cc][0], k0, acc[h]);
+            acc[h] = ffma2(qf[h][cc][1], k1, acc[h]);
+            acc[h] = ffma2(qf[h][cc][2], k2, acc[h]);
+            acc[h] = ffma2(qf[h][cc][3], k3, acc[h]);
+          }
+        }
+        float v[G];
+#pragma unroll
+        for (int h = 0; h < G; ++h) v[h] = acc[h].x + acc[h].y;
+        // reduce-scatter across the 8 lanes of the row group: each halving
+        // step keeps half of the heads; then a butterfly finishes the sum
+#pragma unroll
+        for (int step = 4, cnt = G; step >= 1; step >>= 1) {
+          if (cnt > 1) {
+            const bool upper = (li & step) != 0;
+#pragma unroll
+            for (int j = 0; j < cnt / 2; ++j) {
+              const float send = upper ? v[j] : v[j + cnt / 2];
+              const float keep = upper ? v[j + cnt / 2] : v[j];
+              v[j] = keep + __shfl_xor_sync(0xffffffffu, send, step);
+            }
+            cnt >>= 1;
+          } else {
+            v[0] += __shfl_xor_sync(0xffffffffu, v[0], step);
+          }
+        }
+        sc[pass] = (row < n) ? v[0] : -INFINITY;
+      }
+      // ---- online softmax for head my_head over this sub-tile
+      float mt = sc[0];
+#pragma unroll
+      for (int j = 1; j < kSubTile / 4; ++j) mt = fmaxf(mt, sc[j]);
+      mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 8));
+      mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 16));
+      const float m_new = fmaxf(m_own, mt);
+      const float alpha_own = fast_exp2(m_own - m_new);
+      float ps = 0.f;
+#pragma unroll
+      for (int j = 0; j < kSubTile / 4; ++j) {
+        const float pj = fast_exp2(sc[j] - m_new);
+        ps += pj;
+        if ((li % LPH) == 0) pw[(j * 4 + tg) * G + my_head] = pj;
+      }
+      l_own = l_own * alpha_own + ps;
+      m_own = m_new;
+      float alpha[G];
+#pragma unroll
+      for (int h = 0; h < G; ++h) alpha[h] = __shfl_sync(0xffffffffu, alpha_own, h * LPH);
+      __syncwarp();
+      // ---- P.V for this sub-tile
+#pragma unroll
+      for (int h = 0; h < G; ++h)
+#pragma unroll
+        for (int j = 0; j < DPL / 2; ++j) o[h][j] = fmul2(o[h][j], make_float2(alpha[h], alpha[h]));
+      const int ns = min(kSubTile, n - sub);
+      for (int r = 0; r < ns; ++r) {
+        float pr[G];
+        if constexpr (G % 4 == 0) {
+#pragma unroll
+          for (int h4 = 0; h4 < G; h4 += 4) {
+            const float4 t4 = *reinterpret_cast<const float4*>(pw + r * G + h4);
+            pr[h4] = t4.x; pr[h4 + 1] = t4.y; pr[h4 + 2] = t4.z; pr[h4 + 3] = t4.w;
+          }
+        } else if constexpr (G == 2) {
+          const float2 t2 = *reinterpret_cast<const float2*>(pw + r * G);
+          pr[0] = t2.x; pr[1] = t2.y;
+        } else {
+          pr[0] = pw[r];
+        }
+        const T* vrow = Vs + (sub + r) * D + lane * DPL;
+        float2 vf[DPL / 2];
+        if constexpr (DPL == 8) {
+          const uint4 raw = *reinterpret_cast<const uint4*>(vrow);
+          vf[0] = E::to_float2(raw.x); vf[1] = E::to_float2(raw.y);
+          vf[2] = E::to_float2(raw.z); vf[3] = E::to_float2(raw.w);
+        } else if constexpr (DPL == 4) {
+          const uint2 raw = *reinterpret_cast<const uint2*>(vrow);
+          vf[0] = E::to_float2(raw.x); vf[1] = E::to_float2(raw.y);
+        } else {
+          vf[0] = E::to_float2(*reinterpret_cast<const uint32_t*>(vrow));
+        }
+#pragma unroll
+        for (int h = 0; h < G; ++h)
+#pragma unroll
+          for (int j = 0; j < DPL / 2; ++j) o[h][j] = ffma2(make_float2(pr[h], pr[h]), vf[j], o[h][j]);
+      }
+      __syncwarp();
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[slot]);
+  }
+
+  // ---- combine the consumer warps' states
+  float l_tot = l_own;
+  l_tot += __shfl_xor_sync(0xffffffffu, l_tot, 8);
+  l_tot += __shfl_xor_sync(0xffffffffu, l_tot, 16);
+  if (lane < 8 && (li % LPH) == 0) {
+    comb_m[cw * G + my_head] = alive ? m_own : -INFINITY;
+    comb_l[cw * G + my_head] = alive ? l_tot : 0.f;
+  }
+#pragma unroll
+  for (int h = 0; h < G; ++h)
+#pragma unroll
+    for (int j = 0; j < DPL / 2; ++j)
+      *reinterpret_cast<float2*>(comb_o + (cw * G + h) * D + lane * DPL + 2 * j) = o[h][j];
+  named_bar_sync(1, kConsumerWarps * 32);
+
+  const int ctid = threadIdx.x - 32 * kProducerWarps;
+  for (int e = ctid; e < G * D; e += kConsumerWarps * 32) {
+    const int h = e / D, d = e - h * D;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, comb_m[w * G + h]);
+    float den = 0.f, num = 0.f;
+    if (M != -INFINITY) {
+#pragma unroll
+      for (int w = 0; w < kConsumerWarps; ++w) {
+        const float s = fast_exp2(comb_m[w * G + h] - M);
+        den += s * comb_l[w * G + h];
+        num += s * comb_o[(w * G + h) * D + d];
+      }
+    }
+    const float val = den > 0.f ? num / den : 0.f;
+    if (p.direct_out) {
+      T* out = static_cast<T*>(p.out);
+      out[(int64_t)b * p.o_sb + (int64_t)(head0 + h) * p.o_sh + (int64_t)d * p.o_sd] = E::from_float(val);
+    } else {
+      p.part_o[((int64_t)item * G + h) * D + d] = val;
+      if (d == 0) p.part_lse[(int64_t)item * G + h] = den > 0.f ? M + log2f(den) : -INFINITY;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// merge of split-KV partials: O = sum_j 2^{lse_j - M} O_j / sum_j 2^{lse_j - M}
+// ---------------------------------------------------------------------------
+template <typename T, int D, int G, bool PAGED>
+__global__ void __launch_bounds__(256) decode_merge_kernel(const DecodeParams p) {
+  using E = Elem<T>;
+  const int b = blockIdx.x / p.units;
+  const int unit = blockIdx.x - b * p.units;
+  int c0, c1;
+  if (PAGED) {
+    c0 = p.chunk_offset[b];
+    c1 = p.chunk_offset[b + 1];
+  } else {
+    c0 = b * p.chunks_per_seq;
+    c1 = c0 + p.chunks_per_seq;
+  }
+  const int kvh = unit / p.g_tiles;
+  const int head0 = kvh * p.group + (unit - kvh * p.g_tiles) * G;
+  T* out = static_cast<T*>(p.out);
+  for (int e = threadIdx.x; e < G * D; e += blockDim.x) {
+    const int h = e / D, d = e - h * D;
+    float M = -INFINITY;
+    for (int cc = c0; cc < c1; ++cc) M = fmaxf(M, p.part_lse[((int64_t)cc * p.units + unit) * G + h]);
+    float den = 0.f, num = 0.f;
+    if (M != -INFINITY) {
+      for (int cc = c0; cc < c1; ++cc) {
+        const int64_t it = (int64_t)cc * p.units + unit;
+        const float s = fast_exp2(p.part_lse[it * G + h] - M);
+        den += s;
+        num += s * p.part_o[(it * G + h) * D + d];
+      }
+    }
+    const float val = den > 0.f ? num / den : 0.f;
+    out[(int64_t)b * p.o_sb + (int64_t)(head0 + h) * p.o_sh + (int64_t)d * p.o_sd] = E::from_float(val);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+thread_local std::string g_last_error;
+
+int set_error(int code, const std::string& msg) {
+  g_last_error = msg;
+  return code;
+}
+
+int sm_count() {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  static thread_local int cached_dev = -1, cached = 0;
+  if (dev != cached_dev) {
+    cudaDeviceGetAttribute(&cached, cudaDevAttrMultiProcessorCount, dev);
+    if (cached <= 0) cached = 148;
+    cached_dev = dev;
+  }
+  return cached;
+}
+
+namespace {
+
+struct Plan {
+  int G_tile, tile_tokens, chunk_tokens, num_stages;
+  int64_t items;  // upper bound (paged) or exact (dense)
+  int chunks_per_seq;
+  size_t smem;
+  size_t ws_bytes;
+  size_t off_lse, off_chunk;
+  bool direct;
+};
+
+int pick_group_tile(int group, int D) {
+  const int cap = D >= 256 ? 4 : 8;
+  for (int g = cap; g >= 2; g >>= 1)
+    if (group % g == 0) return g;
+  return 1;
+}
+
+int largest_divisor_le(int n, int cap) {
+  for (int d = std::min(n, cap); d >= 1; --d)
+    if (n % d == 0) return d;
+  return 1;
+}
+
+size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+Plan make_plan(bool paged, int B, int Hq, int Hkv, int D, int L, int P, int64_t num_page_entries,
+               size_t elem_size) {
+  Plan pl{};
+  const int group = Hq / Hkv;
+  pl.G_tile = pick_group_tile(group, D);
+  const int units = Hkv * (group / pl.G_tile);
+  const int tcap = (int)(4096 / D);  // stage of K+V tiles <= 16 KB
+  pl.tile_tokens = paged ? largest_divisor_le(P, tcap) : tcap;
+  const size_t stage_bytes = (size_t)2 * pl.tile_tokens * D * elem_size;
+  pl.num_stages = (int)std::max<size_t>(2, std::min<size_t>(16, (60 * 1024) / stage_bytes));
+  // estimated tiles over all units -> chunk size: aim for ~12 CTAs per SM in
+  // total, but no more than 32 tiles per chunk
+  int64_t tiles_per_unit;
+  if (paged) {
+    tiles_per_unit = num_page_entries * (int64_t)(P / pl.tile_tokens);
+  } else {
+    tiles_per_unit = (int64_t)B * cdiv(L, pl.tile_tokens);
+  }
+  const int64_t total_tiles = std::max<int64_t>(1, tiles_per_unit * units);
+  const int64_t target = (int64_t)sm_count() * 12;
+  int64_t ct = (total_tiles + target - 1) / target;
+  ct = std::max<int64_t>(1, std::min<int64_t>(32, ct));
+  pl.chunk_tokens = (int)(ct * pl.tile_tokens);
+  if (paged) {
+    const int64_t chunks = num_page_entries * (int64_t)P / pl.chunk_tokens + B;
+    pl.items = chunks * units;
+    pl.chunks_per_seq = 0;
+    pl.direct = false;
+  } else {
+    pl.chunks_per_seq = std::max(1, cdiv(L, pl.chunk_tokens));
+    pl.items = (int64_t)B * pl.chunks_per_seq * units;
+    pl.direct = pl.chunks_per_seq == 1;
+  }
+  pl.smem = (size_t)pl.num_stages * stage_bytes +
+            sizeof(float) * ((size_t)kConsumerWarps * pl.G_tile * (2 + D) + (size_t)kConsumerWarps * kSubTile * pl.G_tile) +
+            sizeof(uint64_t) * 2 * pl.num_stages;
+  size_t ws = 0;
+  if (!pl.direct) {
+    ws = align_up((size_t)pl.items * pl.G_tile * D * sizeof(float), 256);
+    pl.off_lse = ws;
+    ws += align_up((size_t)pl.items * pl.G_tile * sizeof(float), 256);
+  }
+  pl.off_chunk = ws;
+  if (paged) ws += align_up((size_t)(B + 1) * sizeof(int), 256);
+  pl.ws_bytes = ws;
+  return pl;
+}
+
+template <typename T, int D, int G, bool PAGED>
+int launch_decode(DecodeParams p, const Plan& pl, cudaStream_t st) {
+  auto kern = decode_splitkv_kernel<T, D, G, PAGED>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl.smem);
+  if (e != cudaSuccess) return set_error(AKT_ERR_CUDA, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
+  if (PAGED) paged_plan_kernel<<<1, 1024, 0, st>>>(p);
+  if (pl.items > 0) {
+    ProfileScope prof(st);
+    kern<<<(unsigned)pl.items, kDecodeThreads, pl.smem, st>>>(p);
+  }
+  if (!pl.direct) {
+    const unsigned nb = (unsigned)p.B * p.units;
+    if (nb > 0) decode_merge_kernel<T, D, G, PAGED><<<nb, 256, 0, st>>>(p);
+  }
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return set_error(AKT_ERR_CUDA, std::string("decode launch: ") + cudaGetErrorString(e));
+  return AKT_OK;
+}
+
+template <typename T, bool PAGED>
+int dispatch_decode(DecodeParams p, const Plan& pl, int D, cudaStream_t st) {
+#define AKT_G(DD)                                                              \
+  switch (pl.G_tile) {                                                         \
+    case 1: return launch_decode<T, DD, 1, PAGED>(p, pl, st);                  \
+    case 2: return launch_decode<T, DD, 2, PAGED>(p, pl, st);                  \
+    case 4: return launch_decode<T, DD, 4, PAGED>(p, pl, st);                  \
+    default: break;                                                            \
+  }
+  switch (D) {
+    case 64:
+      AKT_G(64)
+      if (pl.G_tile == 8) return launch_decode<T, 64, 8, PAGED>(p, pl, st);
+      break;
+    case 128:
+      AKT_G(128)
+      if (pl.G_tile == 8) return launch_decode<T, 128, 8, PAGED>(p, pl, st);
+      break;
+    case 256:
+      AKT_G(256)
+      break;
+  }
+#undef AKT_G
+  return set_error(AKT_ERR_UNSUPPORTED, "decode: head_dim must be 64, 128 or 256");
+}
+
+bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; }
+
+}  // namespace
+
+}  // namespace akt
+
+using namespace akt;
+
+extern "C" {
+
+int akt_abi_version(void) { return AKT_ABI_VERSION; }
+
+const char* akt_last_error(void) { return g_last_error.c_str(); }
+
+int akt_device_status(int device, unsigned int* status_out) {
+  int prev = 0;
+  cudaGetDevice(&prev);
+  cudaError_t e = cudaSetDevice(device);
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  unsigned int v = 0;
+  if (e == cudaSuccess) e = cudaMemcpyFromSymbol(&v, g_device_status, sizeof(v));
+  cudaSetDevice(prev);
+  if (e != cudaSuccess) return set_error(AKT_ERR_CUDA, cudaGetErrorString(e));
+  if (status_out) *status_out = v;
+  return AKT_OK;
+}
+
+int akt_clear_device_status(int device) {
+  int prev = 0;
+  cudaGetDevice(&prev);
+  cudaError_t e = cudaSetDevice(device);
+  unsigned int z = 0;
+  if (e == cudaSuccess) e = cudaMemcpyToSymbol(g_device_status, &z, sizeof(z));
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  cudaSetDevice(prev);
+  if (e != cudaSuccess) return set_error(AKT_ERR_CUDA, cudaGetErrorString(e));
+  return AKT_OK;
+}
+
+static int check_common(int B, int Hq, int Hkv, int D, int dtype) {
+  if (B < 0 || Hq <= 0 || Hkv <= 0) return set_error(AKT_ERR_INVALID, "batch/heads must be positive");
+  if (Hq % Hkv != 0) return set_error(AKT_ERR_INVALID, "num_qo_heads must be a multiple of num_kv_heads");
+  if (D != 64 && D != 128 && D != 256) return set_error(AKT_ERR_UNSUPPORTED, "head_dim must be 64, 128 or 256");
+  if (dtype != AKT_FLOAT16 && dtype != AKT_BFLOAT16) return set_error(AKT_ERR_INVALID, "dtype");
+  return AKT_OK;
+}
+
+size_t akt_decode_dense_workspace_size(const akt_decode_dense_args* a) {
+  if (!a || check_common(a->batch, a->num_qo_heads, a->num_kv_heads, a->head_dim, a->dtype) != AKT_OK) return 0;
+  Plan pl = make_plan(false, a->batch, a->num_qo_heads, a->num_kv_heads, a->head_dim, a->seq_len, 0, 0, 2);
+  return pl.ws_bytes;
+}
+
+int akt_decode_dense(const akt_decode_dense_args* a, void* ws, size_t ws_bytes, void* stream) {
+  if (!a) return set_error(AKT_ERR_INVALID, "null args");
+  int rc = check_common(a->batch, a->num_qo_heads, a->num_kv_heads, a->head_dim, a->dtype);
+  if (rc) return rc;
+  if (a->seq_len < 0) return set_error(AKT_ERR_INVALID, "seq_len < 0");
+  if (a->q_stride_dim != 1 || a->k_stride_dim != 1 || a->v_stride_dim != 1 || a->k_stride_token != a->head_dim ||
+      a->v_stride_token != a->head_dim)
+    return set_error(AKT_ERR_UNSUPPORTED, "decode_dense: K/V rows must be contiguous [.., L, D] and q unit-stride");
+  if (a->k_stride_batch != a->v_stride_batch || a->k_stride_head != a->v_stride_head)
+    return set_error(AKT_ERR_UNSUPPORTED, "decode_dense: K and V must share strides");
+  if (!aligned16(a->q) || !aligned16(a->k) || !aligned16(a->v) || (a->k_stride_batch % 8) || (a->k_stride_head % 8) ||
+      (a->q_stride_batch % 8) || (a->q_stride_head % 8))
+    return set_error(AKT_ERR_UNSUPPORTED, "decode_dense: 16-byte alignment required");
+  if (a->batch == 0) return AKT_OK;
+  Plan pl = make_plan(false, a->batch, a->num_qo_heads, a->num_kv_heads, a->head_dim, a->seq_len, 0, 0, 2);
+  if (pl.ws_bytes > 0 && (!ws || ws_bytes < pl.ws_bytes)) return set_error(AKT_ERR_WORKSPACE, "decode_dense: workspace too small");
+  DecodeParams p{};
+  p.q = a->q; p.q_sb = a->q_stride_batch; p.q_sh = a->q_stride_head;
+  p.k = a->k; p.v = a->v;
+  p.s0 = a->k_stride_batch; p.s_head = a->k_stride_head; p.s_tok = a->k_stride_token;
+  p.out = a->out; p.o_sb = a->out_stride_batch; p.o_sh = a->out_stride_head; p.o_sd = a->out_stride_dim;
+  p.B = a->batch; p.Hq = a->num_qo_heads; p.Hkv = a->num_kv_heads; p.L = a->seq_len; p.P = 0;
+  p.group = p.Hq / p.Hkv; p.g_tiles = p.group / pl.G_tile; p.units = p.Hkv * p.g_tiles;
+  p.tile_tokens = pl.tile_tokens; p.chunk_tokens = pl.chunk_tokens; p.chunks_per_seq = pl.chunks_per_seq;
+  p.num_stages = pl.num_stages; p.scale_log2 = a->softmax_scale * kLog2e;
+  p.direct_out = pl.direct ? 1 : 0;
+  if (!pl.direct) {
+    p.part_o = reinterpret_cast<float*>(ws);
+    p.part_lse = reinterpret_cast<float*>(static_cast<char*>(ws) + pl.off_lse);
+  }
+  if (a->seq_len == 0) {
+    // softmax over no keys: zeros (merge of empty partials)
+    p.chunks_per_seq = 0;
+    Plan z = pl; z.items = 0; z.direct = false;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (a->dtype == AKT_FLOAT16) return dispatch_decode<__half, false>(p, z, a->head_dim, st);
+    return dispatch_decode<__nv_bfloat16, false>(p, z, a->head_dim, st);
+  }
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (a->dtype == AKT_FLOAT16) return dispatch_decode<__half, false>(p, pl, a->head_dim, st);
+  return dispatch_decode<__nv_bfloat16, false>(p, pl, a->head_dim, st);
+}
+
+size_t akt_decode_paged_workspace_size(const akt_decode_paged_args* a) {
+  if (!a || check_common(a->batch, a->num_qo_heads, a->num_kv_heads, a->head_dim, a->dtype) != AKT_OK) return 0;
+  if (a->page_size <= 0) return 0;
+  Plan pl = make_plan(true, a->batch, a->num_qo_heads, a->num_kv_heads, a->head_dim, 0, a->page_size,
+                      a->num_page_entries, 2);
+  return pl.ws_bytes;
+}
+
+int akt_decode_paged(const akt_decode_paged_args* a, void* ws, size_t ws_bytes, void* stream) {
+  if (!a) return set_error(AKT_ERR_INVALID, "null args");
+  int rc = check_common(a->batch, a->num_qo_heads, a->num_kv_heads, a->head_dim, a->dtype);
+  if (rc) return rc;
+  if (a->page_size <= 0) return set_error(AKT_ERR_INVALID, "page_size must be positive");
+  if (a->num_page_entries < 0 || a->num_pages < 0) return set_error(AKT_ERR_INVALID, "negative sizes");
+  if (a->q_stride_dim != 1 || a->kv_stride_dim != 1 || a->kv_stride_token != a->head_dim)
+    return set_error(AKT_ERR_UNSUPPORTED, "decode_paged: page rows must be contiguous [.., P, D] and q unit-stride");
+  if (!aligned16(a->q) || !aligned16(a->kv_cache) || (a->kv_stride_page % 8) || (a->kv_stride_kv % 8) ||
+      (a->kv_stride_head % 8) || (a->q_stride_batch % 8) || (a->q_stride_head % 8))
+    return set_error(AKT_ERR_UNSUPPORTED, "decode_paged: 16-byte alignment required");
+  if (a->batch == 0) return AKT_OK;
+  Plan pl = make_plan(true, a->batch, a->num_qo_heads, a->num_kv_heads, a->head_dim, 0, a->page_size,
+                      a->num_page_entries, 2);
+  if (!ws || ws_bytes < pl.ws_bytes) return set_error(AKT_ERR_WORKSPACE, "decode_paged: workspace too small");
+  DecodeParams p{};
+  p.q = a->q; p.q_sb = a->q_stride_batch; p.q_sh = a->q_stride_head;
+  p.k = a->kv_cache;
+  p.v = static_cast<const char*>(a->kv_cache) + a->kv_stride_kv * 2;
+  p.s0 = a->kv_stride_page; p.s_head = a->kv_stride_head; p.s_tok = a->kv_stride_token;
+  p.indptr = a->kv_page_indptr; p.indices = a->kv_page_indices; p.last_len = a->kv_last_page_len;
+  p.num_pages = a->num_pages; p.num_page_entries = a->num_page_entries;
+  p.out = a->out; p.o_sb = a->out_stride_batch; p.o_sh = a->out_stride_head; p.o_sd = a->out_stride_dim;
+  p.B = a->batch; p.Hq = a->num_qo_heads; p.Hkv = a->num_kv_heads; p.L = 0; p.P = a->page_size;
+  p.group = p.Hq / p.Hkv; p.g_tiles = p.group / pl.G_tile; p.units = p.Hkv * p.g_tiles;
+  p.tile_tokens = pl.tile_tokens; p.chunk_tokens = pl.chunk_tokens; p.chunks_per_seq = 0;
+  p.num_stages = pl.num_stages; p.scale_log2 = a->softmax_scale * kLog2e;
+  p.direct_out = 0;
+  p.part_o = reinterpret_cast<float*>(ws);
+  p.part_lse = reinterpret_cast<float*>(static_cast<char*>(ws) + pl.off_lse);
+  p.chunk_offset = reinterpret_cast<int*>(static_cast<char*>(ws) + pl.off_chunk);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (a->dtype == AKT_FLOAT16) return dispatch_decode<__half, true>(p, pl, a->head_dim, st);
+  return dispatch_decode<__nv_bfloat16, true>(p, pl, a->head_dim, st);
+}
+
+}  // extern "C"

@@ -1,0 +1,289 @@
+"""Benchmark of the headline path: paged var-len GQA decode (BASELINE cfg3).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+One step = one call of ``flash_attention_decode_paged`` over the whole cfg3
+batch (B=64, Hq=32, Hkv=8, D=128, fp16, page size 16, lengths U[512, 32768],
+pages in seeded random physical order), inputs resident in HBM.  The pool is
+4.4 GB, far larger than the 126 MB L2, so no flush is needed between steps.
+
+Multi-GPU (torchrun, one rank per GPU): every rank decodes its own cfg3 batch
+(seed + rank): weak scaling, no data-path collective.  ``value`` is the
+algorithmic bytes of all ranks divided by the max-over-ranks device time.
+
+``--impl reference`` times the reference's naive paged decode (the CPU oracle's
+restatement of ``naive_paged_attention``, fp32 torch on all host cores) on a
+bounded sample of cfg3 sequences, rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+from attention_kernel_triton_b200 import workloads as W  # noqa: E402
+
+METRIC = "paged decode HBM GB/s"
+WORKLOAD = ("cfg3 paged var-len GQA decode: B=64 Hq=32 Hkv=8 D=128 fp16 page_size=16 "
+            "lens U[512,32768] seeded, random physical page order")
+
+
+def measured_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clock/throttle sampling while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except FileNotFoundError:
+            self.proc = None
+        time.sleep(0.3)
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def cpu_reference_step(sample, threads):
+    from oracle import naive as N  # CPU baseline leg only
+    torch.set_num_threads(threads)
+    t0 = time.perf_counter()
+    N.naive_paged_attention(sample["q"], sample["cache"], sample["indptr"], sample["indices"],
+                            sample["last"])
+    return time.perf_counter() - t0
+
+
+def make_cpu_sample(n_seqs: int, seed: int = 0):
+    """A bounded cfg3 sample: the first ``n_seqs`` sequences of the cfg3
+    length distribution, fp32 copies (the CPU oracle computes in fp32)."""
+    lens = torch.randint(512, 32768 + 1, (64,), generator=torch.Generator().manual_seed(seed + 7919)).tolist()
+    c = W.make_paged(lens=lens[:n_seqs], seed=seed)
+    sample = {"q": c.q.float(), "cache": c.cache.float(), "indptr": c.indptr, "indices": c.indices,
+              "last": c.last_page_len}
+    return sample, c.bytes
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    sample, nbytes = make_cpu_sample(args.cpu_seqs)
+    for _ in range(args.warmup):
+        cpu_reference_step(sample, threads)
+    times = [cpu_reference_step(sample, threads) for _ in range(args.steps)]
+    t = statistics.mean(times)
+    val = nbytes / t / 1e9
+    desc = (f"naive_paged_attention restated (oracle port), fp32 torch CPU, first {args.cpu_seqs} "
+            f"cfg3 sequences per step")
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": val, "unit": "GB/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": t * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "sample": desc},
+        "cpu_baseline": {"value": val, "unit": "GB/s", "cores": threads, "kind": "port", "sample": desc},
+        "e2e": {"value": val, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def run_ours(args):
+    from attention_kernel_triton_b200 import _lib
+    from attention_kernel_triton_b200.decode_flash_attention_redundant_var_len_paged import (
+        decode_paged_into, flash_attention_decode_paged)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    pg = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
+        pg = dist
+
+    c = W.make_paged(seed=1000 + rank, device=dev)
+    nbytes = c.bytes
+    out = torch.empty((64, 32, 128), dtype=torch.float16, device=dev)
+
+    def step():
+        decode_paged_into(out, c.q, c.cache, c.indptr, c.indices, c.last_page_len)
+
+    def barrier():
+        if pg is not None:
+            pg.barrier()
+        torch.cuda.synchronize(dev)
+
+    for _ in range(args.warmup):
+        step()
+    barrier()
+
+    clocks = ClockSampler(local)
+    clocks.start()
+    barrier()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with _lib.profile_kernels() as prof:
+        ev0.record()
+        for _ in range(args.steps):
+            step()
+        ev1.record()
+        torch.cuda.synchronize(dev)
+    barrier()
+    clk = clocks.stop()
+    ms = ev0.elapsed_time(ev1)
+    kern_ms = prof.total_ms / max(prof.launches, 1)
+    t = torch.tensor([ms, kern_ms], dtype=torch.float64, device=dev)
+    if pg is not None:
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+    ms, kern_ms = float(t[0]), float(t[1])
+    ms_step = ms / args.steps
+    value = world * nbytes / (ms_step * 1e-3) / 1e9
+
+    # e2e through the public API: per step, the step's inputs (q and the page
+    # table) come from pinned host memory and the output goes back to host.
+    # The KV pool is the resident cache state of the serving loop.
+    h_q = c.q.cpu().pin_memory()
+    h_indptr = c.indptr.cpu().pin_memory()
+    h_indices = c.indices.cpu().pin_memory()
+    h_last = c.last_page_len.cpu().pin_memory()
+    h_out = torch.empty((64, 32, 128), dtype=torch.float16).pin_memory()
+    h2d = sum(x.numel() * x.element_size() for x in (h_q, h_indptr, h_indices, h_last))
+    d2h = h_out.numel() * h_out.element_size()
+    e2e_steps = max(3, min(args.steps, 200))
+
+    def e2e_step():
+        q = h_q.to(dev, non_blocking=True)
+        ip = h_indptr.to(dev, non_blocking=True)
+        ix = h_indices.to(dev, non_blocking=True)
+        la = h_last.to(dev, non_blocking=True)
+        O = flash_attention_decode_paged(q, c.cache, ip, ix, la)
+        h_out.copy_(O, non_blocking=True)
+
+    for _ in range(3):
+        e2e_step()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record()
+    torch.cuda.synchronize(dev)
+    e2e_ms = e0.elapsed_time(e1) / e2e_steps
+    t = torch.tensor([e2e_ms], dtype=torch.float64, device=dev)
+    if pg is not None:
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+    e2e_ms = float(t[0])
+    e2e_val = world * nbytes / (e2e_ms * 1e-3) / 1e9
+
+    peak, peak_kind = measured_peaks()
+    achieved = nbytes / (kern_ms * 1e-3) / 1e9
+    result = None
+    if rank == 0:
+        cpu = None
+        if world == 1 and not args.no_cpu_baseline:
+            threads = os.cpu_count() or 1
+            sample, sbytes = make_cpu_sample(args.cpu_seqs)
+            cpu_reference_step(sample, threads)
+            reps = [cpu_reference_step(sample, threads) for _ in range(2)]
+            cpu_t = statistics.mean(reps)
+            cpu = {"value": sbytes / cpu_t / 1e9, "unit": "GB/s", "cores": threads, "kind": "port",
+                   "sample": f"naive_paged_attention restated (oracle port), fp32 torch CPU, first "
+                             f"{args.cpu_seqs} cfg3 sequences, mean of 2 runs"}
+        result = {
+            "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "fp16", "data": "synthetic",
+            "config": {"workload": WORKLOAD, "bytes_per_step_per_gpu": nbytes,
+                       "l2": "inputs larger than L2 (4.4 GB pool per GPU), no flush",
+                       "parallelism": f"independent batch per GPU x{world}"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "peak_source": peak_kind,
+                         "kernel": "decode_splitkv_kernel<half,128,4,paged>",
+                         "kernel_ms": kern_ms, "traffic": None},
+            "cpu_baseline": cpu,
+            "e2e": {"value": e2e_val, "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "ms_per_step": e2e_ms},
+            "gpu_launches": 3 * args.steps,
+            "clocks": clk,
+        }
+        print(json.dumps(result), flush=True)
+    if pg is not None:
+        pg.barrier()
+        pg.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--cpu-seqs", type=int, default=4)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

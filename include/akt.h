@@ -1,0 +1,118 @@
+/*
+ * akt.h — C ABI of the B200 (sm_100a) attention kernels.
+ *
+ * Plain C: device pointers, element strides and sizes; no torch types.  Every
+ * entry point is asynchronous on the given CUDA stream (a cudaStream_t passed
+ * as void*, NULL = legacy default stream), never synchronises the host, and
+ * returns an akt_status.  On a non-zero return akt_last_error() gives a
+ * message for the calling thread.
+ *
+ * Each entry point replaces the Triton launcher of one reference module of
+ * KiritoHugh/attention_kernel_triton (cited per function).  Tensor shapes and
+ * argument meanings are those of the reference launchers; strides are in
+ * elements.  Out-of-range page ids or token indices never fault: the kernel
+ * skips the access and records a code in the device status word
+ * (akt_device_status).
+ *
+ * Entry points that need scratch take a caller-owned device workspace whose
+ * size the matching *_workspace_size() function returns for the same args.
+ */
+#ifndef AKT_H_
+#define AKT_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define AKT_ABI_VERSION 1
+
+typedef enum akt_status {
+  AKT_OK = 0,
+  AKT_ERR_INVALID = 1,     /* bad shape / argument (the reference asserts) */
+  AKT_ERR_UNSUPPORTED = 2, /* layout the kernel cannot take (caller may copy to contiguous) */
+  AKT_ERR_CUDA = 3,        /* CUDA runtime error (launch, attribute) */
+  AKT_ERR_WORKSPACE = 4    /* workspace missing or too small */
+} akt_status;
+
+typedef enum akt_dtype { AKT_FLOAT16 = 0, AKT_BFLOAT16 = 1 } akt_dtype;
+
+/* ------------------------------------------------------------------------ */
+/* library / device status                                                  */
+/* ------------------------------------------------------------------------ */
+int akt_abi_version(void);
+const char* akt_last_error(void);
+/* First error code any kernel recorded on `device` since the last clear
+ * (0 = none; 1 wait timeout, 2 page id out of pool, 3 token index out of
+ * sequence, 4 malformed indptr).  Synchronises that device. */
+int akt_device_status(int device, unsigned int* status_out);
+int akt_clear_device_status(int device);
+
+/* Benchmark hook: while enabled on the calling thread, each entry point
+ * records a CUDA event pair around its main kernel on the launch stream.
+ * akt_profile_read waits for them, returns the summed device milliseconds
+ * and the number of timed launches, and resets the record. */
+int akt_profile_enable(int on);
+int akt_profile_read(double* total_ms, int64_t* launches);
+
+/* ------------------------------------------------------------------------ */
+/* dense ("redundant") GQA decode                                           */
+/* replaces flash_attention_decode(q, K, V, softmax_scale, GQA_group_size)  */
+/* decode_flash_attention_redundant.py:233-271                              */
+/* ------------------------------------------------------------------------ */
+typedef struct akt_decode_dense_args {
+  const void* q; /* [batch, num_qo_heads, 1, head_dim] */
+  int64_t q_stride_batch, q_stride_head, q_stride_dim;
+  const void* k; /* [batch, num_kv_heads, seq_len, head_dim] */
+  int64_t k_stride_batch, k_stride_head, k_stride_token, k_stride_dim;
+  const void* v; /* [batch, num_kv_heads, seq_len, head_dim] */
+  int64_t v_stride_batch, v_stride_head, v_stride_token, v_stride_dim;
+  void* out; /* [batch, num_qo_heads, 1, head_dim] */
+  int64_t out_stride_batch, out_stride_head, out_stride_dim;
+  int32_t batch, num_qo_heads, num_kv_heads, seq_len, head_dim;
+  int32_t dtype; /* akt_dtype of q, k, v and out */
+  float softmax_scale;
+} akt_decode_dense_args;
+
+size_t akt_decode_dense_workspace_size(const akt_decode_dense_args* args);
+int akt_decode_dense(const akt_decode_dense_args* args, void* workspace, size_t workspace_bytes,
+                     void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* paged var-len GQA decode                                                 */
+/* replaces flash_attention_decode_paged(q, paged_kv_cache, kv_page_indptr, */
+/*   kv_page_indices, kv_last_page_len)                                     */
+/* decode_flash_attention_redundant_var_len_paged.py:228-274                */
+/* Sequence b is pages kv_page_indices[indptr[b] .. indptr[b+1]); its last  */
+/* page holds kv_last_page_len[b] tokens (clamped to [0, page_size]); an    */
+/* empty sequence yields zeros.  softmax_scale is 1/sqrt(head_dim) in the   */
+/* reference (line 244); it is an argument here.                            */
+/* ------------------------------------------------------------------------ */
+typedef struct akt_decode_paged_args {
+  const void* q; /* [batch, num_qo_heads, 1, head_dim] */
+  int64_t q_stride_batch, q_stride_head, q_stride_dim;
+  const void* kv_cache; /* [num_pages, 2, num_kv_heads, page_size, head_dim] */
+  int64_t kv_stride_page, kv_stride_kv, kv_stride_head, kv_stride_token, kv_stride_dim;
+  int64_t num_pages;               /* extent of kv_cache dim 0 (bounds check) */
+  const int32_t* kv_page_indptr;   /* [batch + 1] */
+  const int32_t* kv_page_indices;  /* [num_page_entries] */
+  const int32_t* kv_last_page_len; /* [batch] */
+  int64_t num_page_entries;
+  void* out; /* [batch, num_qo_heads, head_dim] */
+  int64_t out_stride_batch, out_stride_head, out_stride_dim;
+  int32_t batch, num_qo_heads, num_kv_heads, page_size, head_dim;
+  int32_t dtype;
+  float softmax_scale;
+} akt_decode_paged_args;
+
+size_t akt_decode_paged_workspace_size(const akt_decode_paged_args* args);
+int akt_decode_paged(const akt_decode_paged_args* args, void* workspace, size_t workspace_bytes,
+                     void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* AKT_H_ */
