@@ -21,6 +21,7 @@
 //  * CUDA cores only (decode is HBM-bound): q.k with packed fp32x2 FMAs,
 //    an 8-lane reduce-scatter that leaves each lane the score of one
 //    (token, head), exp2 with the scale folded into q, P.V with fp32x2 FMAs.
+#include "attn_core.cuh"
 #include "common.cuh"
 #include "profile.cuh"
 
@@ -36,7 +37,7 @@ __device__ unsigned int g_device_status = 0;
 constexpr int kProducerWarps = 1;
 constexpr int kConsumerWarps = 4;
 constexpr int kDecodeThreads = 32 * (kProducerWarps + kConsumerWarps);
-constexpr int kSubTile = 16;  // tokens per online-softmax step of a consumer warp
+constexpr int kSubTile = kRowsPerSubTile;
 
 struct DecodeParams {
   const void* q;
@@ -133,9 +134,6 @@ template <typename T, int D, int G, bool PAGED>
 __global__ void __launch_bounds__(kDecodeThreads, (G * D > 512) ? 2 : 3) decode_splitkv_kernel(const DecodeParams p) {
   static_assert(D % 64 == 0 && D <= 256, "head_dim");
   static_assert(G == 1 || G == 2 || G == 4 || G == 8, "group tile");
-  constexpr int CH = D / 64;      // 16-byte chunks per lane per token row (8 lanes per row)
-  constexpr int DPL = D / 32;     // output dims per lane in P.V
-  constexpr int LPH = 8 / G;      // lanes sharing one (token, head) score after reduce-scatter
   using E = Elem<T>;
 
   extern __shared__ __align__(128) unsigned char smem[];
@@ -181,6 +179,10 @@ __global__ void __launch_bounds__(kDecodeThreads, (G * D > 512) ? 2 : 3) decode_
   const int kvh = unit / p.g_tiles;
   const int head0 = kvh * p.group + (unit - kvh * p.g_tiles) * G;
 
+  if (NS % kConsumerWarps != 0) {  // host guarantees this; never run a mis-phased ring
+    if (threadIdx.x == 0) record_status(kStatusWaitTimeout);
+    return;
+  }
   if (threadIdx.x == 0) {
     for (int s = 0; s < NS; ++s) {
       mbar_init(&full[s], 1);
@@ -255,195 +257,39 @@ __global__ void __launch_bounds__(kDecodeThreads, (G * D > 512) ? 2 : 3) decode_
 
   // ========================= consumers =========================
   const int cw = warp - kProducerWarps;
-  const int tg = lane >> 3;  // token group within a pass (4 tokens per pass)
-  const int li = lane & 7;   // lane within the 8-lane row group
-  const int my_head = li / LPH;
-
-  // q for the G heads, scaled by softmax_scale*log2(e); lane li holds 16-byte
-  // chunks li, li+8, ... of each row
-  float2 qf[G][CH][4];
-  {
-    const T* qb = static_cast<const T*>(p.q) + (int64_t)b * p.q_sb;
-#pragma unroll
-    for (int h = 0; h < G; ++h) {
-      const T* qh = qb + (int64_t)(head0 + h) * p.q_sh;
-#pragma unroll
-      for (int cc = 0; cc < CH; ++cc) {
-        const uint4 raw = *reinterpret_cast<const uint4*>(qh + (li + 8 * cc) * 8);
-        const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          float2 f = E::to_float2(w[j]);
-          qf[h][cc][j] = make_float2(f.x * p.scale_log2, f.y * p.scale_log2);
-        }
-      }
-    }
-  }
-
-  float m_own = -INFINITY;  // running max (log2 units) of head my_head
-  float l_own = 0.f;        // partial sum of p over this lane's tokens, head my_head
-  float2 o[G][DPL / 2];
-#pragma unroll
-  for (int h = 0; h < G; ++h)
-#pragma unroll
-    for (int j = 0; j < DPL / 2; ++j) o[h][j] = make_float2(0.f, 0.f);
-
+  WarpAttn<T, D, G, false> wa;
+  wa.init(lane);
+  wa.load_q(static_cast<const T*>(p.q) + (int64_t)b * p.q_sb + (int64_t)head0 * p.q_sh, p.q_sh, p.scale_log2);
   float* pw = p_s + cw * kSubTile * G;
   bool alive = true;
+  const ScaledDotScore score;
 
-  for (int t = cw; t < n_tiles && alive; t += kConsumerWarps) {
+  for (int t = cw; t < n_tiles; t += kConsumerWarps) {
     const int slot = t % NS;
-    const uint32_t phase = (uint32_t)(t / NS) & 1u;
-    if (!mbar_wait(&full[slot], phase)) { alive = false; break; }
+    if (!mbar_wait(&full[slot], (uint32_t)(t / NS) & 1u)) { alive = false; break; }
     const int n = min(TT, tok_end - (tok_begin + t * TT));
     const T* Ks = kv_s + (size_t)slot * 2 * stage_elems;
     const T* Vs = Ks + stage_elems;
-
-    for (int sub = 0; sub < n; sub += kSubTile) {
-      float sc[kSubTile / 4];
-#pragma unroll
-      for (int pass = 0; pass < kSubTile / 4; ++pass) {
-        const int row = sub + pass * 4 + tg;
-        const int rr = row < TT ? row : TT - 1;  // stay inside the stage
-        float2 acc[G];
-#pragma unroll
-        for (int h = 0; h < G; ++h) acc[h] = make_float2(0.f, 0.f);
-#pragma unroll
-        for (int cc = 0; cc < CH; ++cc) {
-          const uint4 raw = *reinterpret_cast<const uint4*>(Ks + rr * D + (li + 8 * cc) * 8);
-          const float2 k0 = E::to_float2(raw.x), k1 = E::to_float2(raw.y);
-          const float2 k2 = E::to_float2(raw.z), k3 = E::to_float2(raw.w);
-#pragma unroll
-          for (int h = 0; h < G; ++h) {
-            acc[h] = ffma2(qf[h][cc][0], k0, acc[h]);
-            acc[h] = ffma2(qf[h][cc][1], k1, acc[h]);
-            acc[h] = ffma2(qf[h][cc][2], k2, acc[h]);
-            acc[h] = ffma2(qf[h][cc][3], k3, acc[h]);
-          }
-        }
-        float v[G];
-#pragma unroll
-        for (int h = 0; h < G; ++h) v[h] = acc[h].x + acc[h].y;
-        // reduce-scatter across the 8 lanes of the row group: each halving
-        // step keeps half of the heads; then a butterfly finishes the sum
-#pragma unroll
-        for (int step = 4, cnt = G; step >= 1; step >>= 1) {
-          if (cnt > 1) {
-            const bool upper = (li & step) != 0;
-#pragma unroll
-            for (int j = 0; j < cnt / 2; ++j) {
-              const float send = upper ? v[j] : v[j + cnt / 2];
-              const float keep = upper ? v[j + cnt / 2] : v[j];
-              v[j] = keep + __shfl_xor_sync(0xffffffffu, send, step);
-            }
-            cnt >>= 1;
-          } else {
-            v[0] += __shfl_xor_sync(0xffffffffu, v[0], step);
-          }
-        }
-        sc[pass] = (row < n) ? v[0] : -INFINITY;
-      }
-      // ---- online softmax for head my_head over this sub-tile
-      float mt = sc[0];
-#pragma unroll
-      for (int j = 1; j < kSubTile / 4; ++j) mt = fmaxf(mt, sc[j]);
-      mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 8));
-      mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 16));
-      const float m_new = fmaxf(m_own, mt);
-      const float alpha_own = fast_exp2(m_own - m_new);
-      float ps = 0.f;
-#pragma unroll
-      for (int j = 0; j < kSubTile / 4; ++j) {
-        const float pj = fast_exp2(sc[j] - m_new);
-        ps += pj;
-        if ((li % LPH) == 0) pw[(j * 4 + tg) * G + my_head] = pj;
-      }
-      l_own = l_own * alpha_own + ps;
-      m_own = m_new;
-      float alpha[G];
-#pragma unroll
-      for (int h = 0; h < G; ++h) alpha[h] = __shfl_sync(0xffffffffu, alpha_own, h * LPH);
-      __syncwarp();
-      // ---- P.V for this sub-tile
-#pragma unroll
-      for (int h = 0; h < G; ++h)
-#pragma unroll
-        for (int j = 0; j < DPL / 2; ++j) o[h][j] = fmul2(o[h][j], make_float2(alpha[h], alpha[h]));
-      const int ns = min(kSubTile, n - sub);
-      for (int r = 0; r < ns; ++r) {
-        float pr[G];
-        if constexpr (G % 4 == 0) {
-#pragma unroll
-          for (int h4 = 0; h4 < G; h4 += 4) {
-            const float4 t4 = *reinterpret_cast<const float4*>(pw + r * G + h4);
-            pr[h4] = t4.x; pr[h4 + 1] = t4.y; pr[h4 + 2] = t4.z; pr[h4 + 3] = t4.w;
-          }
-        } else if constexpr (G == 2) {
-          const float2 t2 = *reinterpret_cast<const float2*>(pw + r * G);
-          pr[0] = t2.x; pr[1] = t2.y;
-        } else {
-          pr[0] = pw[r];
-        }
-        const T* vrow = Vs + (sub + r) * D + lane * DPL;
-        float2 vf[DPL / 2];
-        if constexpr (DPL == 8) {
-          const uint4 raw = *reinterpret_cast<const uint4*>(vrow);
-          vf[0] = E::to_float2(raw.x); vf[1] = E::to_float2(raw.y);
-          vf[2] = E::to_float2(raw.z); vf[3] = E::to_float2(raw.w);
-        } else if constexpr (DPL == 4) {
-          const uint2 raw = *reinterpret_cast<const uint2*>(vrow);
-          vf[0] = E::to_float2(raw.x); vf[1] = E::to_float2(raw.y);
-        } else {
-          vf[0] = E::to_float2(*reinterpret_cast<const uint32_t*>(vrow));
-        }
-#pragma unroll
-        for (int h = 0; h < G; ++h)
-#pragma unroll
-          for (int j = 0; j < DPL / 2; ++j) o[h][j] = ffma2(make_float2(pr[h], pr[h]), vf[j], o[h][j]);
-      }
-      __syncwarp();
-    }
+    for (int sub = 0; sub < n; sub += kSubTile)
+      wa.step(Ks, Vs, sub, min(kSubTile, n - sub), TT - 1, 0xffffffffu, pw, score);
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[slot]);
   }
 
   // ---- combine the consumer warps' states
-  float l_tot = l_own;
-  l_tot += __shfl_xor_sync(0xffffffffu, l_tot, 8);
-  l_tot += __shfl_xor_sync(0xffffffffu, l_tot, 16);
-  if (lane < 8 && (li % LPH) == 0) {
-    comb_m[cw * G + my_head] = alive ? m_own : -INFINITY;
-    comb_l[cw * G + my_head] = alive ? l_tot : 0.f;
-  }
-#pragma unroll
-  for (int h = 0; h < G; ++h)
-#pragma unroll
-    for (int j = 0; j < DPL / 2; ++j)
-      *reinterpret_cast<float2*>(comb_o + (cw * G + h) * D + lane * DPL + 2 * j) = o[h][j];
+  wa.stash(comb_m, comb_l, comb_o, cw, alive);
   named_bar_sync(1, kConsumerWarps * 32);
-
   const int ctid = threadIdx.x - 32 * kProducerWarps;
   for (int e = ctid; e < G * D; e += kConsumerWarps * 32) {
     const int h = e / D, d = e - h * D;
-    float M = -INFINITY;
-#pragma unroll
-    for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, comb_m[w * G + h]);
-    float den = 0.f, num = 0.f;
-    if (M != -INFINITY) {
-#pragma unroll
-      for (int w = 0; w < kConsumerWarps; ++w) {
-        const float s = fast_exp2(comb_m[w * G + h] - M);
-        den += s * comb_l[w * G + h];
-        num += s * comb_o[(w * G + h) * D + d];
-      }
-    }
-    const float val = den > 0.f ? num / den : 0.f;
+    float lse2;
+    const float val = combine_warps<kConsumerWarps, G, D>(comb_m, comb_l, comb_o, h, d, lse2);
     if (p.direct_out) {
       T* out = static_cast<T*>(p.out);
       out[(int64_t)b * p.o_sb + (int64_t)(head0 + h) * p.o_sh + (int64_t)d * p.o_sd] = E::from_float(val);
     } else {
       p.part_o[((int64_t)item * G + h) * D + d] = val;
-      if (d == 0) p.part_lse[(int64_t)item * G + h] = den > 0.f ? M + log2f(den) : -INFINITY;
+      if (d == 0) p.part_lse[(int64_t)item * G + h] = lse2;
     }
   }
 }
@@ -543,7 +389,11 @@ Plan make_plan(bool paged, int B, int Hq, int Hkv, int D, int L, int P, int64_t 
   const int tcap = (int)(4096 / D);  // stage of K+V tiles <= 16 KB
   pl.tile_tokens = paged ? largest_divisor_le(P, tcap) : tcap;
   const size_t stage_bytes = (size_t)2 * pl.tile_tokens * D * elem_size;
-  pl.num_stages = (int)std::max<size_t>(2, std::min<size_t>(16, (60 * 1024) / stage_bytes));
+  // Consumer warp w takes tiles w, w+NW, ...; with NS a multiple of NW every
+  // slot has one fixed consumer, so each mbarrier is waited phase by phase
+  // (a parity wait is only unambiguous for the current or previous phase).
+  const size_t fit = (64 * 1024) / stage_bytes;
+  pl.num_stages = (int)std::max<size_t>(kConsumerWarps, std::min<size_t>(16, fit / kConsumerWarps * kConsumerWarps));
   // estimated tiles over all units -> chunk size: aim for ~12 CTAs per SM in
   // total, but no more than 32 tiles per chunk
   int64_t tiles_per_unit;

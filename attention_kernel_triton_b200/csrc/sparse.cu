@@ -1,0 +1,572 @@
+// Sparse-token GQA decode for sm_100a: dense KV, paged KV, and MagicPIG.
+//
+// Replaces the Triton kernels of
+//   sparsetoken_decode_flash_attention_redundant.py:11-124            (dense KV)
+//   sparsetoken_decode_flash_attention_redundant_var_len_paged.py:11-167  (paged KV)
+//   magicpig_sparsetoken_decode_flash_attention_redundant_var_len_paged_with_norm.py:16-164
+// Same math: softmax over the kept tokens sparse_ind[b, h, 0:nnz) only (SD:81-121);
+// paged tokens resolved through the CSR page table (SP:114-126); MagicPIG
+// scores q.k/sqrt(D) - log(u) with u from the LSH collision probability of
+// cos(q, k) (MP:110-148, with the naive reference's clamps, MP:263-278).
+//
+// Machine mapping:
+//  * Work item = (sequence, kv head, group of G qo heads, 32 consecutive list
+//    positions).  A one-CTA planner turns nnz into per-unit chunk counts and
+//    offsets; persistent CTAs walk the item list; a merge kernel combines the
+//    per-chunk (O, log2-sum-exp) partials of each head.
+//  * Gather: each kept row of K and V is one 1-D bulk copy (TMA engine)
+//    HBM->shared, issued by one thread per row, completing one mbarrier.
+//  * GQA: the index lists are per qo head in the API.  When the G heads of an
+//    item carry identical positions (the common case: a per-kv-head keep mask
+//    repeated over the group) the rows are gathered once and all G heads are
+//    computed from them; otherwise each head gathers its own rows.
+//  * Compute: the shared warp core (attn_core.cuh), CUDA cores only.
+#include "attn_core.cuh"
+#include "common.cuh"
+#include "profile.cuh"
+
+#include <algorithm>
+#include <string>
+
+namespace akt {
+
+int set_error(int code, const std::string& msg);
+int sm_count();
+
+namespace {
+
+constexpr int kSW = 4;             // warps per CTA
+constexpr int kSThreads = 32 * kSW;
+constexpr int kCP = 32;            // list positions per work item
+constexpr float kPi = 3.14159265358979323846f;
+
+struct SparseParams {
+  const void* q;
+  int64_t q_sb, q_sh;
+  const void* k;  // dense: K base; paged: pool base
+  const void* v;  // dense: V base; paged: pool base + stride_kv
+  int64_t s0, s_head, s_tok;  // dense: batch/head/token strides; paged: page/head/token
+  const int32_t* indptr;
+  const int32_t* indices;
+  int64_t num_pages, num_page_entries;
+  const int32_t* ind;
+  int64_t ind_sb, ind_sh, ind_sp;
+  const int32_t* nnz;
+  int64_t nnz_sb, nnz_sh;
+  const float* mp_k;
+  const float* mp_l;
+  int64_t par_sb, par_sh;
+  void* out;
+  int64_t o_sb, o_sh, o_sd;
+  int B, Hq, Hkv, L, P, max_nnz;
+  int group, g_tiles, units;  // units per batch = Hkv * g_tiles
+  float scale_log2;
+  float inv_sqrt_d;
+  float* part_o;       // [items, G, D]
+  float* part_lse;     // [items, G]
+  int* unit_offset;    // [B * units + 1]
+};
+
+// ---------------------------------------------------------------------------
+// planner: chunks per (batch, unit) = ceil(max nnz over the unit's heads / kCP)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ int clamped_nnz(const SparseParams& p, int b, int h) {
+  int n = p.nnz[(int64_t)b * p.nnz_sb + (int64_t)h * p.nnz_sh];
+  if (n > p.max_nnz) {
+    record_status(kStatusBadToken);
+    n = p.max_nnz;
+  }
+  return n < 0 ? 0 : n;
+}
+
+template <int G>
+__global__ void __launch_bounds__(1024) sparse_plan_kernel(SparseParams p) {
+  __shared__ int warp_sums[32];
+  __shared__ int carry;
+  if (threadIdx.x == 0) carry = 0;
+  __syncthreads();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int n_units = p.B * p.units;
+  for (int base = 0; base < n_units; base += 1024) {
+    const int u = base + threadIdx.x;
+    int n = 0;
+    if (u < n_units) {
+      const int b = u / p.units, unit = u - b * p.units;
+      const int kvh = unit / p.g_tiles;
+      const int head0 = kvh * p.group + (unit - kvh * p.g_tiles) * G;
+      int mx = 0;
+      for (int h = 0; h < G; ++h) mx = max(mx, clamped_nnz(p, b, head0 + h));
+      n = cdiv(mx, kCP);
+    }
+    int x = n;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, x, o);
+      if (lane >= o) x += y;
+    }
+    if (lane == 31) warp_sums[warp] = x;
+    __syncthreads();
+    if (warp == 0) {
+      int w = warp_sums[lane];
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, w, o);
+        if (lane >= o) w += y;
+      }
+      warp_sums[lane] = w;
+    }
+    __syncthreads();
+    const int incl = x + (warp > 0 ? warp_sums[warp - 1] : 0);
+    if (u < n_units) p.unit_offset[u] = carry + incl - n;
+    __syncthreads();
+    if (threadIdx.x == 1023) carry += incl;
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) p.unit_offset[n_units] = carry;
+}
+
+// ---------------------------------------------------------------------------
+// scores
+// ---------------------------------------------------------------------------
+struct MagicPigScore {
+  float qn;       // |q| of the lane's head
+  float K, Lp;    // LSH parameters of the lane's head
+  float inv_sqrt_d;
+  __device__ __forceinline__ float operator()(float dot, float kk, int) const {
+    const float kn = sqrtf(kk);
+    float c = dot / (qn * kn + 1e-8f);
+    c = fminf(fmaxf(c, -1.0f + 1e-7f), 1.0f - 1e-7f);
+    float pr = 1.0f - (1.0f / kPi) * acosf(c);
+    pr = fminf(fmaxf(pr, 0.0f), 1.0f);
+    const float pK = powf(pr, K);
+    const float omp = fminf(fmaxf(1.0f - pK, 0.0f), 1.0f);
+    float u = 1.0f - powf(omp, Lp) - Lp * pK * powf(omp, Lp - 1.0f);
+    u = fmaxf(u, 1e-10f);
+    return (dot * inv_sqrt_d - logf(u)) * kLog2e;
+  }
+};
+
+// ---------------------------------------------------------------------------
+// shared-memory layout of one CTA
+// ---------------------------------------------------------------------------
+template <typename T, int D, int G>
+struct SparseSmem {
+  static constexpr size_t kv = (size_t)2 * kCP * D * sizeof(T);
+  static constexpr size_t comb = sizeof(float) * ((size_t)kSW * G * (2 + D) + (size_t)kSW * kRowsPerSubTile * G);
+  static constexpr size_t idx = sizeof(int) * ((size_t)G * kCP + G);
+  static constexpr size_t flags = 64;  // kCP row-valid bytes, padded
+  static constexpr size_t bytes = kv + comb + idx + flags + 16;
+};
+
+template <typename T, int D, int G, bool PAGED, bool MAGIC>
+struct SparseCta {
+  using E = Elem<T>;
+  const SparseParams& p;
+  T* Ks;
+  T* Vs;
+  float *comb_m, *comb_l, *comb_o, *p_s;
+  int* idx_s;
+  int* nnz_s;
+  unsigned char* ok_s;
+  uint64_t* bar;
+  int tid, warp, lane;
+  uint32_t phase;
+  uint64_t pol;
+
+  __device__ SparseCta(const SparseParams& p_, unsigned char* smem) : p(p_) {
+    Ks = reinterpret_cast<T*>(smem);
+    Vs = Ks + kCP * D;
+    comb_m = reinterpret_cast<float*>(smem + SparseSmem<T, D, G>::kv);
+    comb_l = comb_m + kSW * G;
+    comb_o = comb_l + kSW * G;
+    p_s = comb_o + kSW * G * D;
+    idx_s = reinterpret_cast<int*>(p_s + kSW * kRowsPerSubTile * G);
+    nnz_s = idx_s + G * kCP;
+    ok_s = reinterpret_cast<unsigned char*>(nnz_s + G);
+    bar = reinterpret_cast<uint64_t*>(ok_s + 64);
+    tid = threadIdx.x;
+    warp = tid >> 5;
+    lane = tid & 31;
+    phase = 0;
+    pol = l2_policy_evict_first();
+  }
+
+  // Gather the K/V rows of list positions rows[0..kCP) (token ids, -1 = none)
+  // into Ks/Vs.  Invalid rows are zero-filled and flagged in ok_s.
+  __device__ bool gather(const int* rows, int b, int kvh) {
+    bool ok = false;
+    int64_t off = 0;
+    if (tid < kCP) {
+      const int tok = rows[tid];
+      if (tok >= 0) {
+        if (PAGED) {
+          const int s = p.indptr[b], e = p.indptr[b + 1];
+          const int npg = e - s;
+          if (s < 0 || npg < 0 || e > p.num_page_entries || tok >= npg * p.P) {
+            record_status(kStatusBadToken);
+          } else {
+            const int pg = tok / p.P;
+            const int phys = __ldg(p.indices + s + pg);
+            if (phys < 0 || (int64_t)phys >= p.num_pages) {
+              record_status(kStatusBadPage);
+            } else {
+              ok = true;
+              off = (int64_t)phys * p.s0 + (int64_t)kvh * p.s_head + (int64_t)(tok - pg * p.P) * p.s_tok;
+            }
+          }
+        } else {
+          if (tok >= p.L) {
+            record_status(kStatusBadToken);
+          } else {
+            ok = true;
+            off = (int64_t)b * p.s0 + (int64_t)kvh * p.s_head + (int64_t)tok * p.s_tok;
+          }
+        }
+      }
+      ok_s[tid] = ok ? 1 : 0;
+    }
+    const int n_ok = __syncthreads_count(ok);
+    if (tid == 0) mbar_arrive_expect_tx(bar, (uint32_t)n_ok * 2u * D * sizeof(T));
+    // zero-fill rows that get no copy so masked rows stay finite in P.V
+    for (int e = tid; e < kCP * D / 8; e += kSThreads) {
+      const int r = e / (D / 8);
+      if (!ok_s[r]) {
+        reinterpret_cast<uint4*>(Ks)[e] = make_uint4(0, 0, 0, 0);
+        reinterpret_cast<uint4*>(Vs)[e] = make_uint4(0, 0, 0, 0);
+      }
+    }
+    __syncthreads();
+    if (ok) {
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      const T* kb = static_cast<const T*>(p.k);
+      const T* vb = static_cast<const T*>(p.v);
+      bulk_g2s(Ks + tid * D, kb + off, D * sizeof(T), bar, pol);
+      bulk_g2s(Vs + tid * D, vb + off, D * sizeof(T), bar, pol);
+    }
+    bool done = mbar_wait(bar, phase & 1u);
+    if (!done) done = mbar_wait(bar, phase & 1u);  // drain copies in flight before giving up
+    ++phase;
+    return done;
+  }
+
+  // attention of NH heads (head0 + hoff ...) over the gathered rows; writes
+  // the partial of item `item` at head slot hoff.
+  template <int NH>
+  __device__ void compute(int item, int b, int head_first, int hoff) {
+    WarpAttn<T, D, NH, MAGIC> wa;
+    wa.init(lane);
+    const T* q0 = static_cast<const T*>(p.q) + (int64_t)b * p.q_sb + (int64_t)head_first * p.q_sh;
+    wa.load_q(q0, p.q_sh, MAGIC ? 1.0f : p.scale_log2);
+    constexpr int RPW = kCP / kSW;  // rows per warp
+    const int row0 = warp * RPW;
+    const uint32_t bits = __ballot_sync(0xffffffffu, lane < RPW && ok_s[row0 + min(lane, RPW - 1)]);
+    float* pw = p_s + warp * kRowsPerSubTile * G;
+    if constexpr (MAGIC) {
+      const int hq = head_first + wa.my_head;
+      MagicPigScore sc;
+      sc.qn = sqrtf(wa.q_norm2_my_head());
+      sc.K = p.mp_k[(int64_t)b * p.par_sb + (int64_t)hq * p.par_sh];
+      sc.Lp = p.mp_l[(int64_t)b * p.par_sb + (int64_t)hq * p.par_sh];
+      sc.inv_sqrt_d = p.inv_sqrt_d;
+      wa.step(Ks, Vs, row0, RPW, kCP - 1, bits, pw, sc);
+    } else {
+      wa.step(Ks, Vs, row0, RPW, kCP - 1, bits, pw, ScaledDotScore());
+    }
+    wa.stash(comb_m, comb_l, comb_o, warp, true);
+    __syncthreads();
+    for (int e = tid; e < NH * D; e += kSThreads) {
+      const int h = e / D, d = e - h * D;
+      float lse2;
+      const float val = combine_warps<kSW, NH, D>(comb_m, comb_l, comb_o, h, d, lse2);
+      p.part_o[((int64_t)item * G + hoff + h) * D + d] = val;
+      if (d == 0) p.part_lse[(int64_t)item * G + hoff + h] = lse2;
+    }
+    __syncthreads();
+  }
+};
+
+template <typename T, int D, int G, bool PAGED, bool MAGIC>
+__global__ void __launch_bounds__(kSThreads) sparse_decode_kernel(const SparseParams p) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  SparseCta<T, D, G, PAGED, MAGIC> cta(p, smem);
+  if (cta.tid == 0) {
+    mbar_init(cta.bar, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  const int n_units = p.B * p.units;
+  const int total = p.unit_offset[n_units];
+  for (int item = blockIdx.x; item < total; item += gridDim.x) {
+    int lo = 0, hi = n_units - 1;  // largest u with unit_offset[u] <= item
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (p.unit_offset[mid] <= item) lo = mid; else hi = mid - 1;
+    }
+    const int u = lo;
+    const int c = item - p.unit_offset[u];
+    const int b = u / p.units, unit = u - b * p.units;
+    const int kvh = unit / p.g_tiles;
+    const int head0 = kvh * p.group + (unit - kvh * p.g_tiles) * G;
+    const int p0 = c * kCP;
+    if (cta.tid < G) cta.nnz_s[cta.tid] = clamped_nnz(p, b, head0 + cta.tid);
+    __syncthreads();
+    for (int e = cta.tid; e < G * kCP; e += kSThreads) {
+      const int h = e / kCP, j = e - h * kCP;
+      const int pos = p0 + j;
+      cta.idx_s[e] = pos < cta.nnz_s[h]
+                         ? p.ind[(int64_t)b * p.ind_sb + (int64_t)(head0 + h) * p.ind_sh + (int64_t)pos * p.ind_sp]
+                         : -1;
+    }
+    __syncthreads();
+    bool same = true;
+    for (int e = cta.tid; e < (G - 1) * kCP; e += kSThreads) same &= cta.idx_s[kCP + e] == cta.idx_s[e % kCP];
+    const bool packed = __syncthreads_and(same) != 0;
+    if (packed) {
+      if (!cta.gather(cta.idx_s, b, kvh)) return;
+      cta.template compute<G>(item, b, head0, 0);
+    } else {
+      for (int h = 0; h < G; ++h) {
+        if (!cta.gather(cta.idx_s + h * kCP, b, kvh)) return;
+        cta.template compute<1>(item, b, head0 + h, h);
+      }
+    }
+  }
+}
+
+// merge of the per-chunk partials of every (batch, unit): chunks are the
+// contiguous items unit_offset[u] .. unit_offset[u+1)
+template <typename T, int D, int G>
+__global__ void __launch_bounds__(256) sparse_merge_kernel(const SparseParams p) {
+  using E = Elem<T>;
+  const int u = blockIdx.x;
+  const int b = u / p.units, unit = u - b * p.units;
+  const int kvh = unit / p.g_tiles;
+  const int head0 = kvh * p.group + (unit - kvh * p.g_tiles) * G;
+  const int i0 = p.unit_offset[u], i1 = p.unit_offset[u + 1];
+  T* out = static_cast<T*>(p.out);
+  for (int e = threadIdx.x; e < G * D; e += blockDim.x) {
+    const int h = e / D, d = e - h * D;
+    float M = -INFINITY;
+    for (int it = i0; it < i1; ++it) M = fmaxf(M, p.part_lse[(int64_t)it * G + h]);
+    float den = 0.f, num = 0.f;
+    if (M != -INFINITY) {
+      for (int it = i0; it < i1; ++it) {
+        const float s = fast_exp2(p.part_lse[(int64_t)it * G + h] - M);
+        den += s;
+        num += s * p.part_o[((int64_t)it * G + h) * D + d];
+      }
+    }
+    const float val = den > 0.f ? num / den : 0.f;
+    out[(int64_t)b * p.o_sb + (int64_t)(head0 + h) * p.o_sh + (int64_t)d * p.o_sd] = E::from_float(val);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// host
+// ---------------------------------------------------------------------------
+struct SparsePlan {
+  int G_tile, units;
+  int64_t items;  // upper bound
+  size_t smem, ws_bytes, off_lse, off_units;
+  int grid;
+};
+
+int sparse_group_tile(int group, int D) {
+  const int cap = D >= 256 ? 4 : 8;
+  for (int g = cap; g >= 2; g >>= 1)
+    if (group % g == 0) return g;
+  return 1;
+}
+
+size_t al256(size_t x) { return (x + 255) / 256 * 256; }
+
+template <typename T, int D, int G>
+size_t sparse_smem_bytes() {
+  return SparseSmem<T, D, G>::bytes;
+}
+
+SparsePlan make_sparse_plan(int B, int Hq, int Hkv, int D, int max_nnz) {
+  SparsePlan pl{};
+  const int group = Hq / Hkv;
+  pl.G_tile = sparse_group_tile(group, D);
+  pl.units = Hkv * (group / pl.G_tile);
+  pl.items = (int64_t)B * pl.units * cdiv(std::max(max_nnz, 0), kCP);
+  size_t ws = al256((size_t)std::max<int64_t>(pl.items, 1) * pl.G_tile * D * sizeof(float));
+  pl.off_lse = ws;
+  ws += al256((size_t)std::max<int64_t>(pl.items, 1) * pl.G_tile * sizeof(float));
+  pl.off_units = ws;
+  ws += al256(((size_t)B * pl.units + 1) * sizeof(int));
+  pl.ws_bytes = ws;
+  pl.grid = (int)std::max<int64_t>(1, std::min<int64_t>(pl.items, (int64_t)sm_count() * 8));
+  return pl;
+}
+
+template <typename T, int D, int G, bool PAGED, bool MAGIC>
+int launch_sparse(const SparseParams& p, const SparsePlan& pl, cudaStream_t st) {
+  auto kern = sparse_decode_kernel<T, D, G, PAGED, MAGIC>;
+  const size_t smem = SparseSmem<T, D, G>::bytes;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return set_error(AKT_ERR_CUDA, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
+  sparse_plan_kernel<G><<<1, 1024, 0, st>>>(p);
+  if (pl.items > 0) {
+    ProfileScope prof(st);
+    kern<<<pl.grid, kSThreads, smem, st>>>(p);
+  }
+  const unsigned nb = (unsigned)(p.B * p.units);
+  if (nb > 0) sparse_merge_kernel<T, D, G><<<nb, 256, 0, st>>>(p);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return set_error(AKT_ERR_CUDA, std::string("sparse launch: ") + cudaGetErrorString(e));
+  return AKT_OK;
+}
+
+template <typename T, bool PAGED, bool MAGIC>
+int dispatch_sparse(const SparseParams& p, const SparsePlan& pl, int D, cudaStream_t st) {
+  switch (D) {
+    case 64:
+      switch (pl.G_tile) {
+        case 1: return launch_sparse<T, 64, 1, PAGED, MAGIC>(p, pl, st);
+        case 2: return launch_sparse<T, 64, 2, PAGED, MAGIC>(p, pl, st);
+        case 4: return launch_sparse<T, 64, 4, PAGED, MAGIC>(p, pl, st);
+        case 8: return launch_sparse<T, 64, 8, PAGED, MAGIC>(p, pl, st);
+      }
+      break;
+    case 128:
+      switch (pl.G_tile) {
+        case 1: return launch_sparse<T, 128, 1, PAGED, MAGIC>(p, pl, st);
+        case 2: return launch_sparse<T, 128, 2, PAGED, MAGIC>(p, pl, st);
+        case 4: return launch_sparse<T, 128, 4, PAGED, MAGIC>(p, pl, st);
+        case 8: return launch_sparse<T, 128, 8, PAGED, MAGIC>(p, pl, st);
+      }
+      break;
+    case 256:
+      switch (pl.G_tile) {
+        case 1: return launch_sparse<T, 256, 1, PAGED, MAGIC>(p, pl, st);
+        case 2: return launch_sparse<T, 256, 2, PAGED, MAGIC>(p, pl, st);
+        case 4: return launch_sparse<T, 256, 4, PAGED, MAGIC>(p, pl, st);
+      }
+      break;
+  }
+  return set_error(AKT_ERR_UNSUPPORTED, "sparse decode: head_dim must be 64, 128 or 256");
+}
+
+bool al16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; }
+
+int check_heads(int B, int Hq, int Hkv, int D, int dtype, int max_nnz) {
+  if (B < 0 || Hq <= 0 || Hkv <= 0 || max_nnz < 0) return set_error(AKT_ERR_INVALID, "sizes must be non-negative");
+  if (Hq % Hkv != 0) return set_error(AKT_ERR_INVALID, "num_qo_heads must be a multiple of num_kv_heads");
+  if (D != 64 && D != 128 && D != 256) return set_error(AKT_ERR_UNSUPPORTED, "head_dim must be 64, 128 or 256");
+  if (dtype != AKT_FLOAT16 && dtype != AKT_BFLOAT16) return set_error(AKT_ERR_INVALID, "dtype");
+  return AKT_OK;
+}
+
+void fill_common(SparseParams& p, const SparsePlan& pl, void* ws) {
+  p.group = p.Hq / p.Hkv;
+  p.g_tiles = p.group / pl.G_tile;
+  p.units = p.Hkv * p.g_tiles;
+  p.part_o = reinterpret_cast<float*>(ws);
+  p.part_lse = reinterpret_cast<float*>(static_cast<char*>(ws) + pl.off_lse);
+  p.unit_offset = reinterpret_cast<int*>(static_cast<char*>(ws) + pl.off_units);
+}
+
+int paged_entry(const akt_sparse_paged_args* a, void* ws, size_t ws_bytes, void* stream, bool magic) {
+  if (!a) return set_error(AKT_ERR_INVALID, "null args");
+  int rc = check_heads(a->batch, a->num_qo_heads, a->num_kv_heads, a->head_dim, a->dtype, a->max_nnz);
+  if (rc) return rc;
+  if (a->page_size <= 0) return set_error(AKT_ERR_INVALID, "page_size must be positive");
+  if (magic && (!a->magicpig_k || !a->magicpig_l)) return set_error(AKT_ERR_INVALID, "MagicPIG needs K and L");
+  if (a->q_stride_dim != 1 || a->kv_stride_dim != 1)
+    return set_error(AKT_ERR_UNSUPPORTED, "sparse paged: unit dim stride required");
+  if (!al16(a->q) || !al16(a->kv_cache) || (a->kv_stride_page % 8) || (a->kv_stride_kv % 8) ||
+      (a->kv_stride_head % 8) || (a->kv_stride_token % 8) || (a->q_stride_batch % 8) || (a->q_stride_head % 8))
+    return set_error(AKT_ERR_UNSUPPORTED, "sparse paged: 16-byte alignment required");
+  if (a->batch == 0) return AKT_OK;
+  SparsePlan pl = make_sparse_plan(a->batch, a->num_qo_heads, a->num_kv_heads, a->head_dim, a->max_nnz);
+  if (!ws || ws_bytes < pl.ws_bytes) return set_error(AKT_ERR_WORKSPACE, "sparse paged: workspace too small");
+  SparseParams p{};
+  p.q = a->q; p.q_sb = a->q_stride_batch; p.q_sh = a->q_stride_head;
+  p.k = a->kv_cache;
+  p.v = static_cast<const char*>(a->kv_cache) + a->kv_stride_kv * 2;
+  p.s0 = a->kv_stride_page; p.s_head = a->kv_stride_head; p.s_tok = a->kv_stride_token;
+  p.indptr = a->kv_page_indptr; p.indices = a->kv_page_indices;
+  p.num_pages = a->num_pages; p.num_page_entries = a->num_page_entries;
+  p.ind = a->sparse_ind; p.ind_sb = a->ind_stride_batch; p.ind_sh = a->ind_stride_head; p.ind_sp = a->ind_stride_pos;
+  p.nnz = a->sparse_nnz; p.nnz_sb = a->nnz_stride_batch; p.nnz_sh = a->nnz_stride_head;
+  p.mp_k = a->magicpig_k; p.mp_l = a->magicpig_l; p.par_sb = a->param_stride_batch; p.par_sh = a->param_stride_head;
+  p.out = a->out; p.o_sb = a->out_stride_batch; p.o_sh = a->out_stride_head; p.o_sd = a->out_stride_dim;
+  p.B = a->batch; p.Hq = a->num_qo_heads; p.Hkv = a->num_kv_heads; p.L = 0; p.P = a->page_size;
+  p.max_nnz = a->max_nnz;
+  p.scale_log2 = a->softmax_scale * kLog2e;
+  p.inv_sqrt_d = 1.0f / sqrtf((float)a->head_dim);
+  fill_common(p, pl, ws);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (magic) {
+    if (a->dtype == AKT_FLOAT16) return dispatch_sparse<__half, true, true>(p, pl, a->head_dim, st);
+    return dispatch_sparse<__nv_bfloat16, true, true>(p, pl, a->head_dim, st);
+  }
+  if (a->dtype == AKT_FLOAT16) return dispatch_sparse<__half, true, false>(p, pl, a->head_dim, st);
+  return dispatch_sparse<__nv_bfloat16, true, false>(p, pl, a->head_dim, st);
+}
+
+}  // namespace
+}  // namespace akt
+
+using namespace akt;
+
+extern "C" {
+
+size_t akt_sparse_dense_workspace_size(const akt_sparse_dense_args* a) {
+  if (!a || check_heads(a->batch, a->num_qo_heads, a->num_kv_heads, a->head_dim, a->dtype, a->max_nnz)) return 0;
+  return make_sparse_plan(a->batch, a->num_qo_heads, a->num_kv_heads, a->head_dim, a->max_nnz).ws_bytes;
+}
+
+int akt_sparse_dense(const akt_sparse_dense_args* a, void* ws, size_t ws_bytes, void* stream) {
+  if (!a) return set_error(AKT_ERR_INVALID, "null args");
+  int rc = check_heads(a->batch, a->num_qo_heads, a->num_kv_heads, a->head_dim, a->dtype, a->max_nnz);
+  if (rc) return rc;
+  if (a->seq_len < 0) return set_error(AKT_ERR_INVALID, "seq_len < 0");
+  if (a->q_stride_dim != 1 || a->k_stride_dim != 1 || a->v_stride_dim != 1)
+    return set_error(AKT_ERR_UNSUPPORTED, "sparse dense: unit dim stride required");
+  if (a->k_stride_batch != a->v_stride_batch || a->k_stride_head != a->v_stride_head ||
+      a->k_stride_token != a->v_stride_token)
+    return set_error(AKT_ERR_UNSUPPORTED, "sparse dense: K and V must share strides");
+  if (!al16(a->q) || !al16(a->k) || !al16(a->v) || (a->k_stride_batch % 8) || (a->k_stride_head % 8) ||
+      (a->k_stride_token % 8) || (a->q_stride_batch % 8) || (a->q_stride_head % 8))
+    return set_error(AKT_ERR_UNSUPPORTED, "sparse dense: 16-byte alignment required");
+  if (a->batch == 0) return AKT_OK;
+  SparsePlan pl = make_sparse_plan(a->batch, a->num_qo_heads, a->num_kv_heads, a->head_dim, a->max_nnz);
+  if (!ws || ws_bytes < pl.ws_bytes) return set_error(AKT_ERR_WORKSPACE, "sparse dense: workspace too small");
+  SparseParams p{};
+  p.q = a->q; p.q_sb = a->q_stride_batch; p.q_sh = a->q_stride_head;
+  p.k = a->k; p.v = a->v;
+  p.s0 = a->k_stride_batch; p.s_head = a->k_stride_head; p.s_tok = a->k_stride_token;
+  p.ind = a->sparse_ind; p.ind_sb = a->ind_stride_batch; p.ind_sh = a->ind_stride_head; p.ind_sp = a->ind_stride_pos;
+  p.nnz = a->sparse_nnz; p.nnz_sb = a->nnz_stride_batch; p.nnz_sh = a->nnz_stride_head;
+  p.out = a->out; p.o_sb = a->out_stride_batch; p.o_sh = a->out_stride_head; p.o_sd = a->out_stride_dim;
+  p.B = a->batch; p.Hq = a->num_qo_heads; p.Hkv = a->num_kv_heads; p.L = a->seq_len; p.P = 1;
+  p.max_nnz = a->max_nnz;
+  p.scale_log2 = a->softmax_scale * kLog2e;
+  p.inv_sqrt_d = 1.0f / sqrtf((float)a->head_dim);
+  fill_common(p, pl, ws);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (a->dtype == AKT_FLOAT16) return dispatch_sparse<__half, false, false>(p, pl, a->head_dim, st);
+  return dispatch_sparse<__nv_bfloat16, false, false>(p, pl, a->head_dim, st);
+}
+
+size_t akt_sparse_paged_workspace_size(const akt_sparse_paged_args* a) {
+  if (!a || check_heads(a->batch, a->num_qo_heads, a->num_kv_heads, a->head_dim, a->dtype, a->max_nnz)) return 0;
+  return make_sparse_plan(a->batch, a->num_qo_heads, a->num_kv_heads, a->head_dim, a->max_nnz).ws_bytes;
+}
+
+int akt_sparse_paged(const akt_sparse_paged_args* a, void* ws, size_t ws_bytes, void* stream) {
+  return paged_entry(a, ws, ws_bytes, stream, false);
+}
+
+size_t akt_magicpig_paged_workspace_size(const akt_sparse_paged_args* a) {
+  return akt_sparse_paged_workspace_size(a);
+}
+
+int akt_magicpig_paged(const akt_sparse_paged_args* a, void* ws, size_t ws_bytes, void* stream) {
+  return paged_entry(a, ws, ws_bytes, stream, true);
+}
+
+}  // extern "C"

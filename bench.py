@@ -160,9 +160,9 @@ def run_ours(args):
         dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
         pg = dist
 
-    c = W.make_paged(seed=1000 + rank, device=dev)
+    c = W.make_paged(B=args.batch, seed=1000 + rank, device=dev)
     nbytes = c.bytes
-    out = torch.empty((64, 32, 128), dtype=torch.float16, device=dev)
+    out = torch.empty((args.batch, 32, 128), dtype=torch.float16, device=dev)
 
     def step():
         decode_paged_into(out, c.q, c.cache, c.indptr, c.indices, c.last_page_len)
@@ -204,7 +204,7 @@ def run_ours(args):
     h_indptr = c.indptr.cpu().pin_memory()
     h_indices = c.indices.cpu().pin_memory()
     h_last = c.last_page_len.cpu().pin_memory()
-    h_out = torch.empty((64, 32, 128), dtype=torch.float16).pin_memory()
+    h_out = torch.empty((args.batch, 32, 128), dtype=torch.float16).pin_memory()
     h2d = sum(x.numel() * x.element_size() for x in (h_q, h_indptr, h_indices, h_last))
     d2h = h_out.numel() * h_out.element_size()
     e2e_steps = max(3, min(args.steps, 200))
@@ -251,7 +251,8 @@ def run_ours(args):
             "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "fp16", "data": "synthetic",
-            "config": {"workload": WORKLOAD, "bytes_per_step_per_gpu": nbytes,
+            "config": {"workload": WORKLOAD if args.batch == 64 else WORKLOAD.replace("B=64", f"B={args.batch}"),
+                       "bytes_per_step_per_gpu": nbytes,
                        "l2": "inputs larger than L2 (4.4 GB pool per GPU), no flush",
                        "parallelism": f"independent batch per GPU x{world}"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
@@ -277,6 +278,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seqs", type=int, default=4)
+    ap.add_argument("--batch", type=int, default=64,
+                    help="sequences per GPU (64 = cfg3; smaller only for profiler captures)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.impl == "reference":

@@ -111,6 +111,83 @@ size_t akt_decode_paged_workspace_size(const akt_decode_paged_args* args);
 int akt_decode_paged(const akt_decode_paged_args* args, void* workspace, size_t workspace_bytes,
                      void* stream);
 
+/* ------------------------------------------------------------------------ */
+/* sparse-token GQA decode, dense KV                                        */
+/* replaces sparsetoken_flash_attention_decode(q, K, V, sparse_ind,         */
+/*   sparse_nnz, softmax_scale, GQA_group_size)                             */
+/* sparsetoken_decode_flash_attention_redundant.py:127-170                  */
+/* Head h of batch b attends to tokens sparse_ind[b, h, 0:nnz) of its kv    */
+/* head; nnz <= 0 yields zeros.  Token indices outside [0, seq_len) are     */
+/* skipped and recorded in the device status word.                          */
+/* ------------------------------------------------------------------------ */
+typedef struct akt_sparse_dense_args {
+  const void* q; /* [batch, num_qo_heads, 1, head_dim] */
+  int64_t q_stride_batch, q_stride_head, q_stride_dim;
+  const void* k; /* [batch, num_kv_heads, seq_len, head_dim] */
+  int64_t k_stride_batch, k_stride_head, k_stride_token, k_stride_dim;
+  const void* v;
+  int64_t v_stride_batch, v_stride_head, v_stride_token, v_stride_dim;
+  const int32_t* sparse_ind; /* [batch, num_qo_heads, max_nnz], -1 padded */
+  int64_t ind_stride_batch, ind_stride_head, ind_stride_pos;
+  const int32_t* sparse_nnz; /* [batch, num_qo_heads(, 1)] */
+  int64_t nnz_stride_batch, nnz_stride_head;
+  void* out; /* [batch, num_qo_heads, 1, head_dim] */
+  int64_t out_stride_batch, out_stride_head, out_stride_dim;
+  int32_t batch, num_qo_heads, num_kv_heads, seq_len, head_dim, max_nnz;
+  int32_t dtype;
+  float softmax_scale;
+} akt_sparse_dense_args;
+
+size_t akt_sparse_dense_workspace_size(const akt_sparse_dense_args* args);
+int akt_sparse_dense(const akt_sparse_dense_args* args, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* sparse-token GQA decode, paged KV (and the MagicPIG variant)             */
+/* replaces sparsetoken_flash_attention_decode_paged(q, paged_kv_cache,     */
+/*   kv_page_indptr, kv_page_indices, sparse_ind, sparse_nnz)               */
+/* sparsetoken_decode_flash_attention_redundant_var_len_paged.py:170-232    */
+/* Kept token t of sequence b is row t % page_size of physical page         */
+/* kv_page_indices[indptr[b] + t / page_size]; tokens past the sequence's   */
+/* page list are skipped and recorded.  nnz <= 0 yields zeros.              */
+/* ------------------------------------------------------------------------ */
+typedef struct akt_sparse_paged_args {
+  const void* q; /* [batch, num_qo_heads, 1, head_dim] */
+  int64_t q_stride_batch, q_stride_head, q_stride_dim;
+  const void* kv_cache; /* [num_pages, 2, num_kv_heads, page_size, head_dim] */
+  int64_t kv_stride_page, kv_stride_kv, kv_stride_head, kv_stride_token, kv_stride_dim;
+  int64_t num_pages;
+  const int32_t* kv_page_indptr;  /* [batch + 1] */
+  const int32_t* kv_page_indices; /* [num_page_entries] */
+  int64_t num_page_entries;
+  const int32_t* sparse_ind; /* [batch, num_qo_heads, max_nnz] */
+  int64_t ind_stride_batch, ind_stride_head, ind_stride_pos;
+  const int32_t* sparse_nnz; /* [batch, num_qo_heads(, 1)] */
+  int64_t nnz_stride_batch, nnz_stride_head;
+  /* MagicPIG only (NULL otherwise): per-(batch, qo head) LSH parameters K, L (fp32) */
+  const float* magicpig_k;
+  const float* magicpig_l;
+  int64_t param_stride_batch, param_stride_head;
+  void* out; /* [batch, num_qo_heads, head_dim] */
+  int64_t out_stride_batch, out_stride_head, out_stride_dim;
+  int32_t batch, num_qo_heads, num_kv_heads, page_size, head_dim, max_nnz;
+  int32_t dtype;
+  float softmax_scale; /* ignored by the MagicPIG entry point (fixed 1/sqrt(head_dim)) */
+} akt_sparse_paged_args;
+
+size_t akt_sparse_paged_workspace_size(const akt_sparse_paged_args* args);
+int akt_sparse_paged(const akt_sparse_paged_args* args, void* workspace, size_t workspace_bytes, void* stream);
+
+/* MagicPIG sparse-token paged decode with norm                              */
+/* replaces magicpig_sparsetoken_flash_attention_decode_paged(q,             */
+/*   paged_kv_cache, kv_page_indptr, kv_page_indices, sparse_ind,            */
+/*   sparse_nnz, K, L)                                                       */
+/* magicpig_sparsetoken_decode_flash_attention_redundant_var_len_paged_      */
+/*   with_norm.py:166-209: score_i = q.k_i/sqrt(D) - log(u_i),               */
+/*   u_i = 1 - (1-p^K)^L - L p^K (1-p^K)^(L-1), p = 1 - acos(cos(q,k_i))/pi  */
+/*   (clamps as in that file's naive reference, lines 263-278).              */
+size_t akt_magicpig_paged_workspace_size(const akt_sparse_paged_args* args);
+int akt_magicpig_paged(const akt_sparse_paged_args* args, void* workspace, size_t workspace_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
