@@ -63,6 +63,39 @@ class DecodePagedArgs(Structure):
     ]
 
 
+class SparseDenseArgs(Structure):
+    _fields_ = [
+        ("q", c_void_p), ("q_stride_batch", c_int64), ("q_stride_head", c_int64), ("q_stride_dim", c_int64),
+        ("k", c_void_p), ("k_stride_batch", c_int64), ("k_stride_head", c_int64), ("k_stride_token", c_int64),
+        ("k_stride_dim", c_int64),
+        ("v", c_void_p), ("v_stride_batch", c_int64), ("v_stride_head", c_int64), ("v_stride_token", c_int64),
+        ("v_stride_dim", c_int64),
+        ("sparse_ind", c_void_p), ("ind_stride_batch", c_int64), ("ind_stride_head", c_int64),
+        ("ind_stride_pos", c_int64),
+        ("sparse_nnz", c_void_p), ("nnz_stride_batch", c_int64), ("nnz_stride_head", c_int64),
+        ("out", c_void_p), ("out_stride_batch", c_int64), ("out_stride_head", c_int64), ("out_stride_dim", c_int64),
+        ("batch", c_int32), ("num_qo_heads", c_int32), ("num_kv_heads", c_int32), ("seq_len", c_int32),
+        ("head_dim", c_int32), ("max_nnz", c_int32), ("dtype", c_int32), ("softmax_scale", c_float),
+    ]
+
+
+class SparsePagedArgs(Structure):
+    _fields_ = [
+        ("q", c_void_p), ("q_stride_batch", c_int64), ("q_stride_head", c_int64), ("q_stride_dim", c_int64),
+        ("kv_cache", c_void_p), ("kv_stride_page", c_int64), ("kv_stride_kv", c_int64), ("kv_stride_head", c_int64),
+        ("kv_stride_token", c_int64), ("kv_stride_dim", c_int64), ("num_pages", c_int64),
+        ("kv_page_indptr", c_void_p), ("kv_page_indices", c_void_p), ("num_page_entries", c_int64),
+        ("sparse_ind", c_void_p), ("ind_stride_batch", c_int64), ("ind_stride_head", c_int64),
+        ("ind_stride_pos", c_int64),
+        ("sparse_nnz", c_void_p), ("nnz_stride_batch", c_int64), ("nnz_stride_head", c_int64),
+        ("magicpig_k", c_void_p), ("magicpig_l", c_void_p), ("param_stride_batch", c_int64),
+        ("param_stride_head", c_int64),
+        ("out", c_void_p), ("out_stride_batch", c_int64), ("out_stride_head", c_int64), ("out_stride_dim", c_int64),
+        ("batch", c_int32), ("num_qo_heads", c_int32), ("num_kv_heads", c_int32), ("page_size", c_int32),
+        ("head_dim", c_int32), ("max_nnz", c_int32), ("dtype", c_int32), ("softmax_scale", c_float),
+    ]
+
+
 # name -> (restype, argtypes); every function declared in include/akt.h
 SIGNATURES = {
     "akt_abi_version": (c_int, []),
@@ -75,6 +108,12 @@ SIGNATURES = {
     "akt_decode_dense": (c_int, [POINTER(DecodeDenseArgs), c_void_p, c_size_t, c_void_p]),
     "akt_decode_paged_workspace_size": (c_size_t, [POINTER(DecodePagedArgs)]),
     "akt_decode_paged": (c_int, [POINTER(DecodePagedArgs), c_void_p, c_size_t, c_void_p]),
+    "akt_sparse_dense_workspace_size": (c_size_t, [POINTER(SparseDenseArgs)]),
+    "akt_sparse_dense": (c_int, [POINTER(SparseDenseArgs), c_void_p, c_size_t, c_void_p]),
+    "akt_sparse_paged_workspace_size": (c_size_t, [POINTER(SparsePagedArgs)]),
+    "akt_sparse_paged": (c_int, [POINTER(SparsePagedArgs), c_void_p, c_size_t, c_void_p]),
+    "akt_magicpig_paged_workspace_size": (c_size_t, [POINTER(SparsePagedArgs)]),
+    "akt_magicpig_paged": (c_int, [POINTER(SparsePagedArgs), c_void_p, c_size_t, c_void_p]),
 }
 
 _lib = None
@@ -162,3 +201,27 @@ class profile_kernels:
         check(lib().akt_profile_enable(0))
         self.total_ms, self.launches = float(ms.value), int(n.value)
         return False
+
+
+def index_strides(sparse_ind: torch.Tensor, sparse_nnz: torch.Tensor):
+    """(ind batch, head, pos) and (nnz batch, head) element strides; nnz may be [B,H] or [B,H,1]."""
+    if sparse_ind.dim() != 3:
+        raise ValueError("sparse_ind must be [B, Hq, L_max]")
+    if sparse_nnz.dim() not in (2, 3) or (sparse_nnz.dim() == 3 and sparse_nnz.shape[2] != 1):
+        raise ValueError("sparse_nnz must be [B, Hq] or [B, Hq, 1]")
+    return sparse_ind.stride(), (sparse_nnz.stride(0), sparse_nnz.stride(1))
+
+
+def as_int32(t: torch.Tensor, device) -> torch.Tensor:
+    if t.dtype != torch.int32 or t.device != device:
+        t = t.to(device=device, dtype=torch.int32)
+    return t
+
+
+def run_with_layout_retry(call, make_contiguous):
+    """Call the entry point; if it rejects the layout, retry once on contiguous copies."""
+    rc = call()
+    if rc == AKT_ERR_UNSUPPORTED:
+        make_contiguous()
+        rc = call()
+    check(rc)

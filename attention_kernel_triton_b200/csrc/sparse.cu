@@ -183,7 +183,7 @@ struct SparseCta {
     idx_s = reinterpret_cast<int*>(p_s + kSW * kRowsPerSubTile * G);
     nnz_s = idx_s + G * kCP;
     ok_s = reinterpret_cast<unsigned char*>(nnz_s + G);
-    bar = reinterpret_cast<uint64_t*>(ok_s + 64);
+    bar = reinterpret_cast<uint64_t*>((reinterpret_cast<uintptr_t>(ok_s + 64) + 7) & ~uintptr_t(7));
     tid = threadIdx.x;
     warp = tid >> 5;
     lane = tid & 31;
@@ -246,7 +246,7 @@ struct SparseCta {
     bool done = mbar_wait(bar, phase & 1u);
     if (!done) done = mbar_wait(bar, phase & 1u);  // drain copies in flight before giving up
     ++phase;
-    return done;
+    return __syncthreads_and(done) != 0;  // one decision for the whole CTA
   }
 
   // attention of NH heads (head0 + hoff ...) over the gathered rows; writes

@@ -1,0 +1,70 @@
+"""Sparse-token GQA decode over dense K/V -- drop-in for the reference module of the same name.
+
+``sparsetoken_flash_attention_decode`` keeps the reference launcher's
+signature and return shape ``[B, Hq, 1, D]``
+(``sparsetoken_decode_flash_attention_redundant.py:127-170``).  Head ``h`` of
+batch ``b`` attends only to tokens ``sparse_ind[b, h, 0:nnz]`` of kv head
+``h // GQA_group_size``; ``sparse_nnz`` is ``[B, Hq]`` or ``[B, Hq, 1]``.
+``nnz == 0`` gives zeros (the reference kernel would divide 0/0 there).
+Runs the sm_100a gather kernel behind ``akt_sparse_dense``.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _lib
+
+redundant_len = 16  # reference module constant (SD:7)
+
+
+def sparse_dense_into(out, q, K, V, sparse_ind, sparse_nnz, softmax_scale, GQA_group_size):
+    dev = _lib.require_cuda(q, K, V, out)
+    if not (q.dtype == K.dtype == V.dtype == out.dtype):
+        raise TypeError("q, K, V and the output must share one dtype")
+    B, Hq, _, D = q.shape
+    Hkv = K.shape[1]
+    assert Hq % Hkv == 0
+    assert Hq // Hkv == GQA_group_size
+    ind = _lib.as_int32(sparse_ind, dev)
+    nnz = _lib.as_int32(sparse_nnz, dev)
+    t = {"q": q, "K": K, "V": V}
+    L = _lib.lib()
+
+    def call():
+        a = _lib.SparseDenseArgs()
+        qq, KK, VV = t["q"], t["K"], t["V"]
+        a.q = qq.data_ptr()
+        a.q_stride_batch, a.q_stride_head, a.q_stride_dim = qq.stride(0), qq.stride(1), qq.stride(3)
+        a.k = KK.data_ptr()
+        a.k_stride_batch, a.k_stride_head, a.k_stride_token, a.k_stride_dim = KK.stride()
+        a.v = VV.data_ptr()
+        a.v_stride_batch, a.v_stride_head, a.v_stride_token, a.v_stride_dim = VV.stride()
+        (a.ind_stride_batch, a.ind_stride_head, a.ind_stride_pos), (a.nnz_stride_batch, a.nnz_stride_head) = \
+            _lib.index_strides(ind, nnz)
+        a.sparse_ind, a.sparse_nnz = ind.data_ptr(), nnz.data_ptr()
+        a.out = out.data_ptr()
+        a.out_stride_batch, a.out_stride_head, a.out_stride_dim = out.stride(0), out.stride(1), out.stride(3)
+        a.batch, a.num_qo_heads, a.num_kv_heads, a.seq_len, a.head_dim = B, Hq, Hkv, KK.shape[2], D
+        a.max_nnz = ind.shape[2]
+        a.dtype = _lib.dtype_code(qq)
+        a.softmax_scale = float(softmax_scale)
+        ws = _lib.workspace(L.akt_sparse_dense_workspace_size(ctypes.byref(a)), dev)
+        return L.akt_sparse_dense(ctypes.byref(a), ws.data_ptr(), ws.numel(), _lib.stream_ptr(dev))
+
+    def contiguous():
+        for k in t:
+            t[k] = t[k].contiguous()
+
+    with torch.cuda.device(dev):
+        _lib.run_with_layout_retry(call, contiguous)
+    return out
+
+
+def sparsetoken_flash_attention_decode(q, K, V, sparse_ind, sparse_nnz, softmax_scale, GQA_group_size):
+    """q [B,Hq,1,D], K/V [B,Hkv,S,D], sparse_ind [B,Hq,L_max] (-1 padded), sparse_nnz [B,Hq(,1)]
+    -> O [B, Hq, 1, D] in q.dtype."""
+    B, Hq, _, D = q.shape
+    O = torch.empty((B, Hq, 1, D), dtype=q.dtype, device=q.device)
+    return sparse_dense_into(O, q, K, V, sparse_ind, sparse_nnz, softmax_scale, GQA_group_size)

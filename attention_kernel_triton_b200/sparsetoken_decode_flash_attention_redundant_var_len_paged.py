@@ -1,0 +1,85 @@
+"""Sparse-token GQA decode over a paged KV cache -- drop-in for the reference module of the same name.
+
+``sparsetoken_flash_attention_decode_paged`` keeps the reference launcher's
+signature and return shape ``[B, Hq, D]``
+(``sparsetoken_decode_flash_attention_redundant_var_len_paged.py:170-232``):
+kept token ``t`` of sequence ``b`` is row ``t % page_size`` of physical page
+``kv_page_indices[kv_page_indptr[b] + t // page_size]``; the scale is
+``1/sqrt(D)``; ``nnz == 0`` gives zeros.  Runs the sm_100a gather kernel behind
+``akt_sparse_paged``.
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+
+import torch
+
+from . import _lib
+
+redundant_len = 16  # reference module constant (SP:7)
+
+
+def sparse_paged_call(entry, out, q, paged_kv_cache, kv_page_indptr, kv_page_indices, sparse_ind, sparse_nnz,
+                      softmax_scale, K=None, L=None):
+    dev = _lib.require_cuda(q, paged_kv_cache, out)
+    if not (q.dtype == paged_kv_cache.dtype == out.dtype):
+        raise TypeError("q, paged_kv_cache and the output must share one dtype")
+    B, Hq, one, D = q.shape
+    if paged_kv_cache.dim() != 5 or paged_kv_cache.shape[1] != 2 or paged_kv_cache.shape[4] != D:
+        raise ValueError("paged_kv_cache must be [num_pages, 2, Hkv, page_size, D]")
+    indptr = _lib.as_int32(kv_page_indptr, dev)
+    indices = _lib.as_int32(kv_page_indices, dev)
+    ind = _lib.as_int32(sparse_ind, dev)
+    nnz = _lib.as_int32(sparse_nnz, dev)
+    t = {"q": q, "cache": paged_kv_cache}
+    if K is not None:
+        t["K"] = K.to(device=dev, dtype=torch.float32)
+        t["L"] = L.to(device=dev, dtype=torch.float32)
+    lib = _lib.lib()
+    fn = getattr(lib, entry)
+    wsfn = getattr(lib, entry + "_workspace_size")
+
+    def call():
+        a = _lib.SparsePagedArgs()
+        qq, cache = t["q"], t["cache"]
+        a.q = qq.data_ptr()
+        a.q_stride_batch, a.q_stride_head, a.q_stride_dim = qq.stride(0), qq.stride(1), qq.stride(3)
+        a.kv_cache = cache.data_ptr()
+        (a.kv_stride_page, a.kv_stride_kv, a.kv_stride_head, a.kv_stride_token, a.kv_stride_dim) = cache.stride()
+        a.num_pages = cache.shape[0]
+        a.kv_page_indptr, a.kv_page_indices, a.num_page_entries = indptr.data_ptr(), indices.data_ptr(), indices.numel()
+        (a.ind_stride_batch, a.ind_stride_head, a.ind_stride_pos), (a.nnz_stride_batch, a.nnz_stride_head) = \
+            _lib.index_strides(ind, nnz)
+        a.sparse_ind, a.sparse_nnz = ind.data_ptr(), nnz.data_ptr()
+        if "K" in t:
+            a.magicpig_k, a.magicpig_l = t["K"].data_ptr(), t["L"].data_ptr()
+            if t["K"].shape != (B, Hq) or t["K"].stride() != t["L"].stride():
+                t["K"], t["L"] = t["K"].reshape(B, Hq).contiguous(), t["L"].reshape(B, Hq).contiguous()
+                a.magicpig_k, a.magicpig_l = t["K"].data_ptr(), t["L"].data_ptr()
+            a.param_stride_batch, a.param_stride_head = t["K"].stride()
+        a.out = out.data_ptr()
+        a.out_stride_batch, a.out_stride_head, a.out_stride_dim = out.stride()
+        a.batch, a.num_qo_heads, a.num_kv_heads = B, Hq, cache.shape[2]
+        a.page_size, a.head_dim, a.max_nnz = cache.shape[3], D, ind.shape[2]
+        a.dtype = _lib.dtype_code(qq)
+        a.softmax_scale = float(softmax_scale)
+        ws = _lib.workspace(wsfn(ctypes.byref(a)), dev)
+        return fn(ctypes.byref(a), ws.data_ptr(), ws.numel(), _lib.stream_ptr(dev))
+
+    def contiguous():
+        t["q"], t["cache"] = t["q"].contiguous(), t["cache"].contiguous()
+
+    with torch.cuda.device(dev):
+        _lib.run_with_layout_retry(call, contiguous)
+    return out
+
+
+def sparsetoken_flash_attention_decode_paged(q, paged_kv_cache, kv_page_indptr, kv_page_indices, sparse_ind,
+                                             sparse_nnz):
+    """q [B,Hq,1,D], paged_kv_cache [pages,2,Hkv,P,D], CSR page table, sparse_ind [B,Hq,L_max],
+    sparse_nnz [B,Hq(,1)] -> O [B, Hq, D] in q.dtype."""
+    B, Hq, _, D = q.shape
+    O = torch.empty((B, Hq, D), dtype=q.dtype, device=q.device)
+    return sparse_paged_call("akt_sparse_paged", O, q, paged_kv_cache, kv_page_indptr, kv_page_indices, sparse_ind,
+                             sparse_nnz, 1.0 / math.sqrt(D))
