@@ -62,6 +62,8 @@ struct WarpAttn {
   }
 
   // |q_h|^2 of head my_head (fp32 sum of squares of the loaded q, mult=1)
+  // (each head's partial sums are reduced over the 8 lanes of the row group
+  // before the lane picks its own head)
   __device__ __forceinline__ float q_norm2_my_head() const {
     float s = 0.f;
 #pragma unroll
@@ -71,11 +73,11 @@ struct WarpAttn {
       for (int cc = 0; cc < CH; ++cc)
 #pragma unroll
         for (int j = 0; j < 4; ++j) t += qf[h][cc][j].x * qf[h][cc][j].x + qf[h][cc][j].y * qf[h][cc][j].y;
+      t += __shfl_xor_sync(0xffffffffu, t, 1);
+      t += __shfl_xor_sync(0xffffffffu, t, 2);
+      t += __shfl_xor_sync(0xffffffffu, t, 4);
       if (h == my_head) s = t;
     }
-    s += __shfl_xor_sync(0xffffffffu, s, 1);
-    s += __shfl_xor_sync(0xffffffffu, s, 2);
-    s += __shfl_xor_sync(0xffffffffu, s, 4);
     return s;
   }
 
@@ -170,7 +172,18 @@ struct WarpAttn {
     for (int h = 0; h < G; ++h)
 #pragma unroll
       for (int j = 0; j < DPL / 2; ++j) o[h][j] = fmul2(o[h][j], make_float2(alpha[h], alpha[h]));
-    for (int r = 0; r < ns; ++r) {
+    if (ns == kRowsPerSubTile) {
+#pragma unroll
+      for (int r = 0; r < kRowsPerSubTile; ++r) pv_row(Vs, pw, row0, r);
+    } else {
+      for (int r = 0; r < ns; ++r) pv_row(Vs, pw, row0, r);
+    }
+    __syncwarp();
+  }
+
+  // o[h] += p[r][h] * V[row0 + r] for this lane's dims
+  __device__ __forceinline__ void pv_row(const T* Vs, const float* pw, int row0, int r) {
+    {
       float pr[G];
       if constexpr (G % 4 == 0) {
 #pragma unroll
@@ -201,7 +214,6 @@ struct WarpAttn {
 #pragma unroll
         for (int j = 0; j < DPL / 2; ++j) o[h][j] = ffma2(make_float2(pr[h], pr[h]), vf[j], o[h][j]);
     }
-    __syncwarp();
   }
 
   // Write this warp's state to the CTA combine buffers (index w).

@@ -159,23 +159,11 @@ struct Elem<__nv_bfloat16> {
   }
 };
 
-// packed fp32x2 fused multiply-add (sm_100): d = a * b + c, two lanes at once
-__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
-  uint64_t ua = *reinterpret_cast<uint64_t*>(&a);
-  uint64_t ub = *reinterpret_cast<uint64_t*>(&b);
-  uint64_t uc = *reinterpret_cast<uint64_t*>(&c);
-  uint64_t d;
-  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(ua), "l"(ub), "l"(uc));
-  return *reinterpret_cast<float2*>(&d);
-}
+// packed fp32x2 fused multiply-add / multiply (sm_100 compiler builtins: the
+// operands stay in register pairs, no repacking around the instruction)
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
 
-__device__ __forceinline__ float2 fmul2(float2 a, float2 b) {
-  uint64_t ua = *reinterpret_cast<uint64_t*>(&a);
-  uint64_t ub = *reinterpret_cast<uint64_t*>(&b);
-  uint64_t d;
-  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(ua), "l"(ub));
-  return *reinterpret_cast<float2*>(&d);
-}
+__device__ __forceinline__ float2 fmul2(float2 a, float2 b) { return __fmul2_rn(a, b); }
 
 __device__ __forceinline__ float fast_exp2(float x) {
   float y;

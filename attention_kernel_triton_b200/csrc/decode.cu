@@ -27,6 +27,7 @@
 
 #include <algorithm>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <string>
 
@@ -365,6 +366,20 @@ struct Plan {
   bool direct;
 };
 
+// Tuning knobs, read once per process: AKT_DECODE_STAGE_KB (shared-memory
+// budget of the K/V stage ring per CTA, default 64) and AKT_DECODE_CHUNK_TILES
+// (upper bound on tiles per split-KV chunk, default 128).
+int env_int(const char* name, int dflt) {
+  static thread_local int cache_stage = -1, cache_chunk = -1;
+  int* slot = name[11] == 'S' ? &cache_stage : &cache_chunk;
+  if (*slot < 0) {
+    const char* v = getenv(name);
+    const int x = v ? atoi(v) : 0;
+    *slot = x > 0 ? x : dflt;
+  }
+  return *slot;
+}
+
 int pick_group_tile(int group, int D) {
   const int cap = D >= 256 ? 4 : 8;
   for (int g = cap; g >= 2; g >>= 1)
@@ -392,7 +407,7 @@ Plan make_plan(bool paged, int B, int Hq, int Hkv, int D, int L, int P, int64_t 
   // Consumer warp w takes tiles w, w+NW, ...; with NS a multiple of NW every
   // slot has one fixed consumer, so each mbarrier is waited phase by phase
   // (a parity wait is only unambiguous for the current or previous phase).
-  const size_t fit = (64 * 1024) / stage_bytes;
+  const size_t fit = (size_t)env_int("AKT_DECODE_STAGE_KB", 64) * 1024 / stage_bytes;
   pl.num_stages = (int)std::max<size_t>(kConsumerWarps, std::min<size_t>(16, fit / kConsumerWarps * kConsumerWarps));
   // estimated tiles over all units -> chunk size: aim for ~12 CTAs per SM in
   // total, but no more than 32 tiles per chunk
@@ -405,7 +420,7 @@ Plan make_plan(bool paged, int B, int Hq, int Hkv, int D, int L, int P, int64_t 
   const int64_t total_tiles = std::max<int64_t>(1, tiles_per_unit * units);
   const int64_t target = (int64_t)sm_count() * 12;
   int64_t ct = (total_tiles + target - 1) / target;
-  ct = std::max<int64_t>(1, std::min<int64_t>(32, ct));
+  ct = std::max<int64_t>(1, std::min<int64_t>(env_int("AKT_DECODE_CHUNK_TILES", 128), ct));
   pl.chunk_tokens = (int)(ct * pl.tile_tokens);
   if (paged) {
     const int64_t chunks = num_page_entries * (int64_t)P / pl.chunk_tokens + B;
@@ -618,3 +633,4 @@ int akt_decode_paged(const akt_decode_paged_args* a, void* ws, size_t ws_bytes, 
 }
 
 }  // extern "C"
+
