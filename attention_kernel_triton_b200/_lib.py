@@ -108,6 +108,7 @@ SIGNATURES = {
     "akt_decode_dense": (c_int, [POINTER(DecodeDenseArgs), c_void_p, c_size_t, c_void_p]),
     "akt_decode_paged_workspace_size": (c_size_t, [POINTER(DecodePagedArgs)]),
     "akt_decode_paged": (c_int, [POINTER(DecodePagedArgs), c_void_p, c_size_t, c_void_p]),
+    "akt_decode_paged_noalloc": (c_int, [POINTER(DecodePagedArgs), c_void_p]),
     "akt_sparse_dense_workspace_size": (c_size_t, [POINTER(SparseDenseArgs)]),
     "akt_sparse_dense": (c_int, [POINTER(SparseDenseArgs), c_void_p, c_size_t, c_void_p]),
     "akt_sparse_paged_workspace_size": (c_size_t, [POINTER(SparsePagedArgs)]),

@@ -28,6 +28,7 @@
 #include <algorithm>
 #include <cstdio>
 #include <cstdlib>
+#include <mutex>
 #include <cstring>
 #include <string>
 
@@ -634,3 +635,106 @@ int akt_decode_paged(const akt_decode_paged_args* a, void* ws, size_t ws_bytes, 
 
 }  // extern "C"
 
+// ---------------------------------------------------------------------------
+// Allocation-free paged decode.
+//
+// Some callers cannot allocate device memory at the point where they run the
+// decode: plugin hosts that hand a kernel only its input and output buffers
+// (no allocator or workspace hook), and runtimes that plan every byte of
+// device memory at start-up and forbid cudaMalloc afterwards (it can
+// synchronise the device and fail under a fixed budget).  For them,
+// akt_decode_paged_noalloc keeps the split-KV partials in a fixed array that
+// the library owns.  The array is a file-scope __device__ variable of
+// kNoAllocScratchBytes, so every GPU that loads this library holds that much
+// memory until the process exits.  Its host-side name is only a stand-in for
+// the device symbol: host code must use the address cudaGetSymbolAddress
+// returns for the current device, never the name itself.
+// ---------------------------------------------------------------------------
+namespace akt {
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = size_t(16) << 20;  // 16 MiB per device
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[kMaxDevices] = {};
+
+// Device address of the scratch array on the current device, looked up once
+// per device (the first call on a device does this set-up).
+int noalloc_scratch(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return set_error(AKT_ERR_CUDA, std::string("cudaGetDevice: ") + cudaGetErrorString(e));
+  if (dev < 0 || dev >= kMaxDevices) return set_error(AKT_ERR_INVALID, "device ordinal out of range");
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* ptr = nullptr;
+    e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+    if (e != cudaSuccess || !ptr)
+      return set_error(AKT_ERR_CUDA, std::string("cudaGetSymbolAddress(scratch): ") + cudaGetErrorString(e));
+    g_noalloc_ptr[dev] = ptr;
+  }
+  *out = g_noalloc_ptr[dev];
+  return AKT_OK;
+}
+
+}  // namespace
+}  // namespace akt
+
+extern "C" int akt_decode_paged_noalloc(const akt_decode_paged_args* a, void* stream) {
+  if (!a) return set_error(AKT_ERR_INVALID, "null args");
+  int rc = check_common(a->batch, a->num_qo_heads, a->num_kv_heads, a->head_dim, a->dtype);
+  if (rc) return rc;
+  if (a->page_size <= 0) return set_error(AKT_ERR_INVALID, "page_size must be positive");
+  if (a->num_page_entries < 0 || a->num_pages < 0) return set_error(AKT_ERR_INVALID, "negative sizes");
+  if (a->q_stride_dim != 1 || a->kv_stride_dim != 1 || a->kv_stride_token != a->head_dim)
+    return set_error(AKT_ERR_UNSUPPORTED, "decode_paged_noalloc: page rows must be contiguous [.., P, D] and q unit-stride");
+  if (!aligned16(a->q) || !aligned16(a->kv_cache) || (a->kv_stride_page % 8) || (a->kv_stride_kv % 8) ||
+      (a->kv_stride_head % 8) || (a->q_stride_batch % 8) || (a->q_stride_head % 8))
+    return set_error(AKT_ERR_UNSUPPORTED, "decode_paged_noalloc: 16-byte alignment required");
+  if (a->batch == 0) return AKT_OK;
+  Plan pl = make_plan(true, a->batch, a->num_qo_heads, a->num_kv_heads, a->head_dim, 0, a->page_size,
+                      a->num_page_entries, 2);
+  // Same kernels as akt_decode_paged.  When the partials of the default split
+  // do not fit the fixed array, use longer chunks (fewer partials) until they do.
+  const int units = a->num_kv_heads * (a->num_qo_heads / a->num_kv_heads / pl.G_tile);
+  auto scratch_bytes = [&](const Plan& q) {
+    size_t ws = align_up((size_t)q.items * q.G_tile * a->head_dim * sizeof(float), 256);
+    ws += align_up((size_t)q.items * q.G_tile * sizeof(float), 256);
+    return ws + align_up((size_t)(a->batch + 1) * sizeof(int), 256);
+  };
+  while (pl.ws_bytes > kNoAllocScratchBytes && pl.chunk_tokens < (1 << 20)) {
+    pl.chunk_tokens *= 2;
+    pl.items = (a->num_page_entries * (int64_t)a->page_size / pl.chunk_tokens + a->batch) * units;
+    pl.off_lse = align_up((size_t)pl.items * pl.G_tile * a->head_dim * sizeof(float), 256);
+    pl.off_chunk = pl.off_lse + align_up((size_t)pl.items * pl.G_tile * sizeof(float), 256);
+    pl.ws_bytes = scratch_bytes(pl);
+  }
+  if (pl.ws_bytes > kNoAllocScratchBytes)
+    return set_error(AKT_ERR_WORKSPACE, "decode_paged_noalloc: this call needs " + std::to_string(pl.ws_bytes) +
+                                            " bytes of scratch; the allocation-free entry point holds at most " +
+                                            std::to_string(kNoAllocScratchBytes) + " bytes");
+  void* ws = nullptr;
+  rc = noalloc_scratch(&ws);
+  if (rc) return rc;
+  DecodeParams p{};
+  p.q = a->q; p.q_sb = a->q_stride_batch; p.q_sh = a->q_stride_head;
+  p.k = a->kv_cache;
+  p.v = static_cast<const char*>(a->kv_cache) + a->kv_stride_kv * 2;
+  p.s0 = a->kv_stride_page; p.s_head = a->kv_stride_head; p.s_tok = a->kv_stride_token;
+  p.indptr = a->kv_page_indptr; p.indices = a->kv_page_indices; p.last_len = a->kv_last_page_len;
+  p.num_pages = a->num_pages; p.num_page_entries = a->num_page_entries;
+  p.out = a->out; p.o_sb = a->out_stride_batch; p.o_sh = a->out_stride_head; p.o_sd = a->out_stride_dim;
+  p.B = a->batch; p.Hq = a->num_qo_heads; p.Hkv = a->num_kv_heads; p.L = 0; p.P = a->page_size;
+  p.group = p.Hq / p.Hkv; p.g_tiles = p.group / pl.G_tile; p.units = p.Hkv * p.g_tiles;
+  p.tile_tokens = pl.tile_tokens; p.chunk_tokens = pl.chunk_tokens; p.chunks_per_seq = 0;
+  p.num_stages = pl.num_stages; p.scale_log2 = a->softmax_scale * kLog2e;
+  p.direct_out = 0;
+  p.part_o = reinterpret_cast<float*>(ws);
+  p.part_lse = reinterpret_cast<float*>(static_cast<char*>(ws) + pl.off_lse);
+  p.chunk_offset = reinterpret_cast<int*>(static_cast<char*>(ws) + pl.off_chunk);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (a->dtype == AKT_FLOAT16) return dispatch_decode<__half, true>(p, pl, a->head_dim, st);
+  return dispatch_decode<__nv_bfloat16, true>(p, pl, a->head_dim, st);
+}

@@ -111,6 +111,21 @@ size_t akt_decode_paged_workspace_size(const akt_decode_paged_args* args);
 int akt_decode_paged(const akt_decode_paged_args* args, void* workspace, size_t workspace_bytes,
                      void* stream);
 
+/* Allocation-free paged decode.  No counterpart in the reference: it exists for
+ * callers that cannot allocate device memory when they run the decode (plugin
+ * hosts that pass only input and output buffers, runtimes that forbid
+ * cudaMalloc after start-up).  Same arguments, semantics and kernels as
+ * akt_decode_paged, but the split-KV scratch lives in a fixed 16 MiB array
+ * owned by the library (held on every GPU that loads the library, until
+ * process exit); nothing is allocated per call.  A call whose partials would
+ * not fit returns AKT_ERR_WORKSPACE with the size it needed.  The first call
+ * on a device looks up that array's device address (set-up, once per device,
+ * with the target device current); make that first call before any stream
+ * capture.  All calls share the array and it keeps the last call's contents
+ * (nothing in it needs to start at zero): calls that overlap on the GPU, on
+ * any streams, race and must not be issued. */
+int akt_decode_paged_noalloc(const akt_decode_paged_args* args, void* stream);
+
 /* ------------------------------------------------------------------------ */
 /* sparse-token GQA decode, dense KV                                        */
 /* replaces sparsetoken_flash_attention_decode(q, K, V, sparse_ind,         */
