@@ -10,6 +10,8 @@ import sys
 
 # reference module name -> submodule of this package
 DROPIN_MODULES = (
+    "prefill_flash_attention",
+    "prefill_flash_attention_var_len_padding",
     "decode_flash_attention_redundant",
     "decode_flash_attention_redundant_var_len_paged",
     "sparsetoken_decode_flash_attention_redundant",

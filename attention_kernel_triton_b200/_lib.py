@@ -96,6 +96,22 @@ class SparsePagedArgs(Structure):
     ]
 
 
+class PrefillArgs(Structure):
+    _fields_ = [
+        ("q", c_void_p), ("q_stride_batch", c_int64), ("q_stride_head", c_int64), ("q_stride_token", c_int64),
+        ("q_stride_dim", c_int64),
+        ("k", c_void_p), ("k_stride_batch", c_int64), ("k_stride_head", c_int64), ("k_stride_token", c_int64),
+        ("k_stride_dim", c_int64),
+        ("v", c_void_p), ("v_stride_batch", c_int64), ("v_stride_head", c_int64), ("v_stride_token", c_int64),
+        ("v_stride_dim", c_int64),
+        ("out", c_void_p), ("out_stride_batch", c_int64), ("out_stride_head", c_int64),
+        ("out_stride_token", c_int64), ("out_stride_dim", c_int64),
+        ("varlen", c_void_p),
+        ("batch", c_int32), ("num_qo_heads", c_int32), ("num_kv_heads", c_int32), ("seq_len", c_int32),
+        ("head_dim", c_int32), ("causal", c_int32), ("dtype", c_int32), ("softmax_scale", c_float),
+    ]
+
+
 # name -> (restype, argtypes); every function declared in include/akt.h
 SIGNATURES = {
     "akt_abi_version": (c_int, []),
@@ -104,6 +120,7 @@ SIGNATURES = {
     "akt_clear_device_status": (c_int, [c_int]),
     "akt_profile_enable": (c_int, [c_int]),
     "akt_profile_read": (c_int, [POINTER(ctypes.c_double), POINTER(c_int64)]),
+    "akt_prefill": (c_int, [POINTER(PrefillArgs), c_void_p]),
     "akt_decode_dense_workspace_size": (c_size_t, [POINTER(DecodeDenseArgs)]),
     "akt_decode_dense": (c_int, [POINTER(DecodeDenseArgs), c_void_p, c_size_t, c_void_p]),
     "akt_decode_paged_workspace_size": (c_size_t, [POINTER(DecodePagedArgs)]),

@@ -1,0 +1,525 @@
+// Causal / non-causal GQA prefill (flash-attention forward) for sm_100a on the
+// 5th-generation tensor cores (tcgen05 + TMEM), with padded var-len support.
+//
+// Replaces the Triton kernels of prefill_flash_attention.py:109-335 and
+// prefill_flash_attention_var_len_padding.py:109-341.  Same math:
+// O = softmax(Q K^T * s [+ top-left causal mask]) V with GQA kv head h / G,
+// fp32 accumulation, P rounded to the input dtype before P.V (PF:94); the
+// var-len variant skips query rows past each sequence's length (PV:186-187)
+// and masks no keys (the reference does not either).
+//
+// One CTA = one 128-row query tile of one (batch, head).  Warp roles:
+//   warps 0-3  softmax warpgroup: thread t owns query row t = TMEM lane t;
+//              reads S with tcgen05.ld, writes P (input dtype) to shared
+//              memory in the 128B-swizzled K-major layout, rescales O in
+//              TMEM when its running max moves, and runs the epilogue.
+//   warp 4     TMA producer: Q once, then K_j and V_j into a ring of stages.
+//   warp 5     TMEM allocator and single-thread MMA issuer:
+//              S_j = Q K_j^T  (M=128, N=128, K=D)   into TMEM S[j%2]
+//              O  += P_j V_j  (M=128, N=D,  K=128)  into TMEM O
+// The running max used for exponentiation only moves when the row max grows
+// by more than 8 (log2 units), so O is rescaled rarely (P <= 2^8 stays exact
+// enough in fp16/bf16 relative terms; the final O/l is unchanged).
+#include "common.cuh"
+#include "profile.cuh"
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+#include <string>
+
+namespace akt {
+
+int set_error(int code, const std::string& msg);
+
+namespace {
+
+constexpr int BM = 128;            // query rows per CTA
+constexpr int BN = 128;            // keys per tile
+constexpr int kThreads = 192;
+constexpr int kTmemCols = 512;
+constexpr int kColS0 = 0, kColS1 = 128, kColO = 256;
+constexpr float kRescaleThreshold = 8.0f;  // log2 units
+
+template <int D>
+struct Cfg {
+  static constexpr int DB = D / 64;                       // 64-element (128 B) swizzle blocks per row
+  static constexpr int NSTAGE = D == 64 ? 3 : 2;          // K/V ring
+  static constexpr int NP = D == 64 ? 2 : 1;              // P buffers
+  static constexpr uint32_t Q_BYTES = BM * D * 2;
+  static constexpr uint32_t KV_BYTES = BN * D * 2;        // one of K or V
+  static constexpr uint32_t P_BYTES = BM * BN * 2;
+  static constexpr uint32_t OFF_Q = 0;
+  static constexpr uint32_t OFF_K = OFF_Q + Q_BYTES;
+  static constexpr uint32_t OFF_V = OFF_K + NSTAGE * KV_BYTES;
+  static constexpr uint32_t OFF_P = OFF_V + NSTAGE * KV_BYTES;
+  static constexpr uint32_t OFF_BAR = OFF_P + NP * P_BYTES;
+  static constexpr uint32_t SMEM = OFF_BAR + 256 + 1024;  // + barriers, + alignment slack
+};
+
+struct PrefillParams {
+  void* o;
+  int64_t o_sb, o_sh, o_ss;  // element strides (dim stride 1)
+  const int32_t* varlen;     // [B] or null
+  int B, Hq, Hkv, S, group;
+  int n_q_tiles;
+  int causal;
+  float scale_log2;
+};
+
+// -------------------------------------------------------------------------
+// PTX helpers
+// -------------------------------------------------------------------------
+__device__ __forceinline__ uint64_t desc_sw128(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
+  d |= (uint64_t)1 << 46;  // descriptor version for sm_100
+  d |= (uint64_t)2 << 61;  // 128-byte swizzle
+  return d;
+}
+
+__host__ __device__ constexpr uint32_t idesc_f16(int fmt, int M, int N, int b_mn_major) {
+  return (1u << 4) | ((uint32_t)fmt << 7) | ((uint32_t)fmt << 10) | ((uint32_t)b_mn_major << 16) |
+         ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_f16(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc)
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,"
+      "%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,"
+      "%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]),
+      "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]),
+      "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+__device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, int x, int y, int z, int w,
+                                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5, %6}], "
+      "[%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z), "r"(w)
+      : "memory");
+}
+
+template <typename T>
+__device__ __forceinline__ uint32_t pack_p(float a, float b) {
+  return Elem<T>::pack2(a, b);
+}
+
+// -------------------------------------------------------------------------
+// kernel
+// -------------------------------------------------------------------------
+template <typename T, int D>
+__global__ void __launch_bounds__(kThreads, 1)
+    prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                       const __grid_constant__ CUtensorMap tmV, const PrefillParams p) {
+  using C = Cfg<D>;
+  constexpr int fmt = std::is_same<T, __half>::value ? 0 : 1;
+  constexpr uint32_t IDESC_S = idesc_f16(fmt, BM, BN, 0);
+  constexpr uint32_t IDESC_PV = idesc_f16(fmt, BM, D, 1);
+
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
+  uint64_t* q_full = bars + 0;
+  uint64_t* k_full = bars + 1;                   // [NSTAGE]
+  uint64_t* v_full = k_full + C::NSTAGE;         // [NSTAGE]
+  uint64_t* kv_empty = v_full + C::NSTAGE;       // [NSTAGE]
+  uint64_t* s_full = kv_empty + C::NSTAGE;       // [2]
+  uint64_t* s_empty = s_full + 2;                // [2]
+  uint64_t* p_full = s_empty + 2;                // [NP]
+  uint64_t* p_empty = p_full + C::NP;            // [NP]
+  uint64_t* o_done = p_empty + C::NP;            // 1
+  uint64_t* mma_idle = o_done + 1;               // 1
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_idle + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int q_tile = p.n_q_tiles - 1 - (int)blockIdx.x;  // heaviest causal tiles first
+  const int h = blockIdx.y, b = blockIdx.z;
+  const int q0 = q_tile * BM;
+  const int seq_len = p.varlen ? min(max(p.varlen[b], 0), p.S) : p.S;
+
+  // ---- tile entirely past the sequence (var-len padding): zeros, no MMA
+  if (q0 >= seq_len) {
+    T* o = static_cast<T*>(p.o) + (int64_t)b * p.o_sb + (int64_t)h * p.o_sh;
+    for (int e = threadIdx.x; e < BM * (D / 8); e += kThreads) {
+      const int r = q0 + e / (D / 8), c = (e % (D / 8)) * 8;
+      if (r < p.S) *reinterpret_cast<uint4*>(o + (int64_t)r * p.o_ss + c) = make_uint4(0, 0, 0, 0);
+    }
+    return;
+  }
+  const int last_key = p.causal ? min(q0 + BM, seq_len) - 1 : p.S - 1;  // causal: rows past seq_len are zeroed
+  const int n_kv = last_key / BN + 1;
+  const int kvh = h / p.group;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < C::NSTAGE; ++s) {
+      mbar_init(&k_full[s], 1);
+      mbar_init(&v_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&s_full[s], 1);
+      mbar_init(&s_empty[s], 4);
+    }
+    for (int s = 0; s < C::NP; ++s) {
+      mbar_init(&p_full[s], 4);
+      mbar_init(&p_empty[s], 1);
+    }
+    mbar_init(o_done, 1);
+    mbar_init(mma_idle, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 5) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(kTmemCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  auto wait = [&](uint64_t* bar, uint32_t parity) -> bool {
+    if (*abort_flag) return false;
+    if (mbar_wait(bar, parity)) return true;
+    *abort_flag = 1;
+    return false;
+  };
+
+  if (warp == 4) {
+    // ========================= TMA producer =========================
+    if (lane == 0) {
+      unsigned char* sQ = smem + C::OFF_Q;
+      mbar_arrive_expect_tx(q_full, C::Q_BYTES);
+#pragma unroll
+      for (int db = 0; db < C::DB; ++db) tma_load_4d(sQ + db * BM * 128, &tmQ, db * 64, q0, h, b, q_full);
+      int issued = 0;
+      for (int j = 0; j < n_kv; ++j) {
+        const int st = j % C::NSTAGE;
+        if (j >= C::NSTAGE && !wait(&kv_empty[st], ((j / C::NSTAGE) - 1) & 1)) break;
+        unsigned char* sK = smem + C::OFF_K + st * C::KV_BYTES;
+        unsigned char* sV = smem + C::OFF_V + st * C::KV_BYTES;
+        mbar_arrive_expect_tx(&k_full[st], C::KV_BYTES);
+#pragma unroll
+        for (int db = 0; db < C::DB; ++db) tma_load_4d(sK + db * BN * 128, &tmK, db * 64, j * BN, kvh, b, &k_full[st]);
+        mbar_arrive_expect_tx(&v_full[st], C::KV_BYTES);
+#pragma unroll
+        for (int db = 0; db < C::DB; ++db) tma_load_4d(sV + db * BN * 128, &tmV, db * 64, j * BN, kvh, b, &v_full[st]);
+        issued = j + 1;
+      }
+      if (*abort_flag) {  // drain loads still in flight into this CTA's shared memory
+        mbar_wait(q_full, 0);
+        for (int j = max(0, issued - C::NSTAGE); j < issued; ++j) {
+          mbar_wait(&k_full[j % C::NSTAGE], (j / C::NSTAGE) & 1);
+          mbar_wait(&v_full[j % C::NSTAGE], (j / C::NSTAGE) & 1);
+        }
+      }
+    }
+  } else if (warp == 5) {
+    // ========================= MMA issuer =========================
+    if (lane == 0) {
+      const uint32_t sQ = smem_u32(smem + C::OFF_Q);
+      bool ok = wait(q_full, 0);
+      tc_fence_after();
+      for (int j = 0; ok && j <= n_kv; ++j) {
+        if (j < n_kv) {
+          const int st = j % C::NSTAGE, sb = j & 1;
+          if (!wait(&k_full[st], (j / C::NSTAGE) & 1)) break;
+          if (j >= 2 && !wait(&s_empty[sb], ((j >> 1) - 1) & 1)) break;
+          tc_fence_after();
+          const uint32_t sK = smem_u32(smem + C::OFF_K + st * C::KV_BYTES);
+#pragma unroll
+          for (int k = 0; k < D / 16; ++k) {
+            const uint32_t off = (k >> 2) * (BM * 128) + (k & 3) * 32;
+            const uint32_t offk = (k >> 2) * (BN * 128) + (k & 3) * 32;
+            mma_f16(tmem + (sb ? kColS1 : kColS0), desc_sw128(sQ + off, 16, 1024), desc_sw128(sK + offk, 16, 1024),
+                    IDESC_S, k > 0);
+          }
+          mma_commit(&s_full[sb]);
+        }
+        if (j >= 1) {
+          const int i = j - 1, pb = i % C::NP, st = i % C::NSTAGE;
+          if (!wait(&p_full[pb], (i / C::NP) & 1)) break;
+          if (!wait(&v_full[st], (i / C::NSTAGE) & 1)) break;
+          tc_fence_after();
+          const uint32_t sP = smem_u32(smem + C::OFF_P + pb * C::P_BYTES);
+          const uint32_t sV = smem_u32(smem + C::OFF_V + st * C::KV_BYTES);
+#pragma unroll
+          for (int k = 0; k < BN / 16; ++k) {
+            const uint32_t offp = (k >> 2) * (BM * 128) + (k & 3) * 32;
+            mma_f16(tmem + kColO, desc_sw128(sP + offp, 16, 1024), desc_sw128(sV + k * 2048, BN * 128, 1024),
+                    IDESC_PV, (i > 0 || k > 0) ? 1u : 0u);
+          }
+          mma_commit(o_done);
+          mma_commit(&p_empty[pb]);
+          mma_commit(&kv_empty[st]);
+        }
+      }
+      // every MMA issued by this thread has finished before the CTA can exit
+      mma_commit(mma_idle);
+      mbar_wait(mma_idle, 0);
+    }
+  } else {
+    // ========================= softmax warpgroup =========================
+    const int t = threadIdx.x;  // 0..127: row t of the tile, TMEM lane t
+    const int row = q0 + t;
+    const uint32_t lane_addr = (uint32_t)(warp * 32) << 16;
+    float m_use = -INFINITY, l = 0.f;
+    int pv_seen = 0;
+    bool ok = true;
+    for (int j = 0; j < n_kv; ++j) {
+      const int sb = j & 1, pb = j % C::NP;
+      if (!wait(&s_full[sb], (j >> 1) & 1)) { ok = false; break; }
+      tc_fence_after();
+      float x[BN];
+#pragma unroll
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(tmem + lane_addr + (sb ? kColS1 : kColS0) + c * 32, r);
+        tmem_wait_ld();
+#pragma unroll
+        for (int e = 0; e < 32; ++e) x[c * 32 + e] = __uint_as_float(r[e]);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s_empty[sb]);
+      // scale, mask, row max
+      const int col0 = j * BN;
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < BN; ++c) {
+        const int col = col0 + c;
+        const bool masked = (p.causal && col > row) || col >= p.S;
+        x[c] = masked ? -INFINITY : x[c] * p.scale_log2;
+        mx = fmaxf(mx, x[c]);
+      }
+      const float m_new = fmaxf(m_use, mx);
+      const bool need = m_new > m_use + kRescaleThreshold || (m_use == -INFINITY && m_new != -INFINITY);
+      float alpha = 1.f;
+      if (need) {
+        alpha = fast_exp2(m_use - m_new);
+        m_use = m_new;
+      }
+      const float m_sub = m_use == -INFINITY ? 0.f : m_use;
+      // P = 2^(x - m) in the input dtype, into the swizzled K-major P tile
+      if (j >= C::NP && !wait(&p_empty[pb], ((j / C::NP) - 1) & 1)) { ok = false; break; }
+      unsigned char* sP = smem + C::OFF_P + pb * C::P_BYTES;
+      float rs = 0.f;
+#pragma unroll
+      for (int ch = 0; ch < BN / 8; ++ch) {
+        float pv[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          pv[e] = fast_exp2(x[ch * 8 + e] - m_sub);
+          rs += pv[e];
+        }
+        uint4 w;
+        w.x = pack_p<T>(pv[0], pv[1]);
+        w.y = pack_p<T>(pv[2], pv[3]);
+        w.z = pack_p<T>(pv[4], pv[5]);
+        w.w = pack_p<T>(pv[6], pv[7]);
+        const int kb = ch >> 3, cin = ch & 7;
+        *reinterpret_cast<uint4*>(sP + kb * (BM * 128) + t * 128 + ((cin ^ (t & 7)) << 4)) = w;
+      }
+      l = l * alpha + rs;
+      // O must see PV_{j-1} finished before it is rescaled or before PV_j is queued
+      if (j >= 1) {
+        while (pv_seen < j) {
+          if (!wait(o_done, pv_seen & 1)) { ok = false; break; }
+          ++pv_seen;
+        }
+        if (!ok) break;
+        if (__any_sync(0xffffffffu, need)) {
+          tc_fence_after();
+#pragma unroll
+          for (int c = 0; c < D / 32; ++c) {
+            uint32_t r[32];
+            tmem_ld32(tmem + lane_addr + kColO + c * 32, r);
+            tmem_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * alpha);
+            tmem_st32(tmem + lane_addr + kColO + c * 32, r);
+          }
+          tmem_wait_st();
+        }
+      }
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[pb]);
+    }
+    // ---- epilogue: O / l for valid rows, zeros for var-len padding rows
+    if (ok) {
+      while (pv_seen < n_kv) {
+        if (!wait(o_done, pv_seen & 1)) { ok = false; break; }
+        ++pv_seen;
+      }
+    }
+    T* orow = static_cast<T*>(p.o) + (int64_t)b * p.o_sb + (int64_t)h * p.o_sh + (int64_t)row * p.o_ss;
+    const float inv = (ok && l > 0.f && row < seq_len) ? 1.f / l : 0.f;
+    tc_fence_after();
+#pragma unroll
+    for (int c = 0; c < D / 32; ++c) {
+      uint32_t r[32];
+      tmem_ld32(tmem + lane_addr + kColO + c * 32, r);
+      tmem_wait_ld();
+      if (row < p.S) {
+#pragma unroll
+        for (int e = 0; e < 32; e += 8) {
+          uint4 w;
+          w.x = Elem<T>::pack2(__uint_as_float(r[e + 0]) * inv, __uint_as_float(r[e + 1]) * inv);
+          w.y = Elem<T>::pack2(__uint_as_float(r[e + 2]) * inv, __uint_as_float(r[e + 3]) * inv);
+          w.z = Elem<T>::pack2(__uint_as_float(r[e + 4]) * inv, __uint_as_float(r[e + 5]) * inv);
+          w.w = Elem<T>::pack2(__uint_as_float(r[e + 6]) * inv, __uint_as_float(r[e + 7]) * inv);
+          *reinterpret_cast<uint4*>(orow + c * 32 + e) = w;
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
+  }
+}
+
+// -------------------------------------------------------------------------
+// host: tensor maps through the driver entry point (no -lcuda)
+// -------------------------------------------------------------------------
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+  });
+  return fn;
+}
+
+// 4-D map over [B][H][S][D] (element strides sb, sh, ss; dim stride 1), box 64 x 128
+int make_map(CUtensorMap* m, const void* base, int dtype, int B, int H, int S, int D, int64_t sb, int64_t sh,
+             int64_t ss) {
+  auto fn = encode_fn();
+  if (!fn) return set_error(AKT_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)S, (cuuint64_t)H, (cuuint64_t)B};
+  cuuint64_t strides[3] = {(cuuint64_t)ss * 2, (cuuint64_t)sh * 2, (cuuint64_t)sb * 2};
+  cuuint32_t box[4] = {64, 128, 1, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = fn(m, dtype == AKT_FLOAT16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4,
+                  const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(AKT_ERR_UNSUPPORTED, "cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
+  return AKT_OK;
+}
+
+template <typename T, int D>
+int launch_prefill(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const PrefillParams& p,
+                   cudaStream_t st) {
+  auto kern = prefill_fwd_kernel<T, D>;
+  const int smem = (int)Cfg<D>::SMEM;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return set_error(AKT_ERR_CUDA, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
+  dim3 grid(p.n_q_tiles, p.Hq, p.B);
+  {
+    ProfileScope prof(st);
+    kern<<<grid, kThreads, smem, st>>>(mq, mk, mv, p);
+  }
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return set_error(AKT_ERR_CUDA, std::string("prefill launch: ") + cudaGetErrorString(e));
+  return AKT_OK;
+}
+
+bool al16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; }
+
+}  // namespace
+}  // namespace akt
+
+using namespace akt;
+
+extern "C" int akt_prefill(const akt_prefill_args* a, void* stream) {
+  if (!a) return set_error(AKT_ERR_INVALID, "null args");
+  if (a->batch < 0 || a->num_qo_heads <= 0 || a->num_kv_heads <= 0 || a->seq_len < 0)
+    return set_error(AKT_ERR_INVALID, "sizes must be non-negative");
+  if (a->num_qo_heads % a->num_kv_heads) return set_error(AKT_ERR_INVALID, "num_qo_heads must be a multiple of num_kv_heads");
+  if (a->head_dim != 64 && a->head_dim != 128) return set_error(AKT_ERR_UNSUPPORTED, "prefill: head_dim must be 64 or 128");
+  if (a->dtype != AKT_FLOAT16 && a->dtype != AKT_BFLOAT16) return set_error(AKT_ERR_INVALID, "dtype");
+  if (a->q_stride_dim != 1 || a->k_stride_dim != 1 || a->v_stride_dim != 1 || a->out_stride_dim != 1)
+    return set_error(AKT_ERR_UNSUPPORTED, "prefill: unit dim stride required");
+  const int64_t strides[] = {a->q_stride_batch, a->q_stride_head, a->q_stride_token, a->k_stride_batch,
+                             a->k_stride_head,  a->k_stride_token, a->v_stride_batch, a->v_stride_head,
+                             a->v_stride_token, a->out_stride_batch, a->out_stride_head, a->out_stride_token};
+  for (int64_t s : strides)
+    if (s % 8) return set_error(AKT_ERR_UNSUPPORTED, "prefill: strides must be multiples of 16 bytes");
+  if (!al16(a->q) || !al16(a->k) || !al16(a->v) || !al16(a->out))
+    return set_error(AKT_ERR_UNSUPPORTED, "prefill: 16-byte alignment required");
+  if (a->batch == 0 || a->seq_len == 0) return AKT_OK;
+  CUtensorMap mq, mk, mv;
+  int rc = make_map(&mq, a->q, a->dtype, a->batch, a->num_qo_heads, a->seq_len, a->head_dim, a->q_stride_batch,
+                    a->q_stride_head, a->q_stride_token);
+  if (!rc) rc = make_map(&mk, a->k, a->dtype, a->batch, a->num_kv_heads, a->seq_len, a->head_dim, a->k_stride_batch,
+                         a->k_stride_head, a->k_stride_token);
+  if (!rc) rc = make_map(&mv, a->v, a->dtype, a->batch, a->num_kv_heads, a->seq_len, a->head_dim, a->v_stride_batch,
+                         a->v_stride_head, a->v_stride_token);
+  if (rc) return rc;
+  PrefillParams p{};
+  p.o = a->out;
+  p.o_sb = a->out_stride_batch; p.o_sh = a->out_stride_head; p.o_ss = a->out_stride_token;
+  p.varlen = a->varlen;
+  p.B = a->batch; p.Hq = a->num_qo_heads; p.Hkv = a->num_kv_heads; p.S = a->seq_len;
+  p.group = p.Hq / p.Hkv;
+  p.n_q_tiles = (a->seq_len + BM - 1) / BM;
+  p.causal = a->causal ? 1 : 0;
+  p.scale_log2 = a->softmax_scale * kLog2e;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (a->dtype == AKT_FLOAT16) {
+    if (a->head_dim == 64) return launch_prefill<__half, 64>(mq, mk, mv, p, st);
+    return launch_prefill<__half, 128>(mq, mk, mv, p, st);
+  }
+  if (a->head_dim == 64) return launch_prefill<__nv_bfloat16, 64>(mq, mk, mv, p, st);
+  return launch_prefill<__nv_bfloat16, 128>(mq, mk, mv, p, st);
+}

@@ -58,6 +58,37 @@ int akt_profile_enable(int on);
 int akt_profile_read(double* total_ms, int64_t* launches);
 
 /* ------------------------------------------------------------------------ */
+/* causal / non-causal GQA prefill, optionally padded var-len               */
+/* replaces flash_attention_prefill(Q, K, V, causal, softmax_scale,         */
+/*   GQA_group_size) of prefill_flash_attention.py:342-383 and              */
+/*   flash_attention_prefill(..., varlen) of                                */
+/*   prefill_flash_attention_var_len_padding.py:348-391                     */
+/* Q/O [batch, num_qo_heads, seq_len, head_dim], K/V [batch, num_kv_heads,  */
+/* seq_len, head_dim]; kv head of qo head h is h / (num_qo_heads /          */
+/* num_kv_heads); causal is top-left aligned (row i sees keys j <= i).      */
+/* varlen (int32 [batch], or NULL): rows i >= varlen[b] are written as      */
+/* zeros; keys are not masked by varlen (as in the reference).  head_dim 64 */
+/* or 128; no workspace.                                                    */
+/* ------------------------------------------------------------------------ */
+typedef struct akt_prefill_args {
+  const void* q;
+  int64_t q_stride_batch, q_stride_head, q_stride_token, q_stride_dim;
+  const void* k;
+  int64_t k_stride_batch, k_stride_head, k_stride_token, k_stride_dim;
+  const void* v;
+  int64_t v_stride_batch, v_stride_head, v_stride_token, v_stride_dim;
+  void* out;
+  int64_t out_stride_batch, out_stride_head, out_stride_token, out_stride_dim;
+  const int32_t* varlen;
+  int32_t batch, num_qo_heads, num_kv_heads, seq_len, head_dim;
+  int32_t causal;
+  int32_t dtype;
+  float softmax_scale;
+} akt_prefill_args;
+
+int akt_prefill(const akt_prefill_args* args, void* stream);
+
+/* ------------------------------------------------------------------------ */
 /* dense ("redundant") GQA decode                                           */
 /* replaces flash_attention_decode(q, K, V, softmax_scale, GQA_group_size)  */
 /* decode_flash_attention_redundant.py:233-271                              */

@@ -45,6 +45,7 @@ def test_abi_version_and_error_string():
 
 
 STRUCTS = {
+    "akt_prefill_args": _lib.PrefillArgs,
     "akt_decode_dense_args": _lib.DecodeDenseArgs,
     "akt_decode_paged_args": _lib.DecodePagedArgs,
     "akt_sparse_dense_args": _lib.SparseDenseArgs,

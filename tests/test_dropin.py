@@ -6,6 +6,10 @@ import attention_kernel_triton_b200 as akt
 
 # reference signatures (DR:233, DP:228, SD:127, SP:170, MP:166)
 EXPECTED = {
+    "prefill_flash_attention": ("flash_attention_prefill",
+                                ["Q", "K", "V", "causal", "softmax_scale", "GQA_group_size"]),
+    "prefill_flash_attention_var_len_padding": (
+        "flash_attention_prefill", ["Q", "K", "V", "causal", "softmax_scale", "GQA_group_size", "varlen"]),
     "decode_flash_attention_redundant": ("flash_attention_decode", ["q", "K", "V", "softmax_scale", "GQA_group_size"]),
     "decode_flash_attention_redundant_var_len_paged": (
         "flash_attention_decode_paged", ["q", "paged_kv_cache", "kv_page_indptr", "kv_page_indices", "kv_last_page_len"]),

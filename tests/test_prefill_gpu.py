@@ -1,0 +1,145 @@
+"""GPU parity of the tcgen05 prefill (causal / non-causal / var-len) against the
+CPU oracle and the reference's golden outputs.
+
+Tolerance: max-abs <= 2e-3 against the fp32 oracle, no NaNs (bf16 adds half a
+bf16 ulp of the reference value).  The kernel rounds P to the input dtype
+before P.V, as the reference does (PF:94); the oracle keeps P in fp32.
+"""
+import math
+
+import pytest
+import torch
+
+from golden_io import load
+from oracle import naive as N
+
+from attention_kernel_triton_b200 import _lib
+from attention_kernel_triton_b200 import workloads as W
+from attention_kernel_triton_b200.prefill_flash_attention import flash_attention_prefill
+from attention_kernel_triton_b200.prefill_flash_attention_var_len_padding import (
+    flash_attention_prefill as flash_attention_prefill_varlen)
+
+pytestmark = pytest.mark.gpu
+TOL = 2e-3
+DEV = "cuda"
+
+
+def check_close(out, ref, dtype=torch.float16):
+    out = out.detach().float().cpu()
+    ref = ref.detach().float().cpu()
+    assert out.shape == ref.shape
+    assert not torch.isnan(out).any()
+    err = (out - ref).abs()
+    bound = TOL + (2.0 ** -8 * ref.abs() if dtype == torch.bfloat16 else 0.0)
+    assert bool((err <= bound).all()), f"max err {err.max().item()} at {divmod(int(err.argmax()), out.shape[-1])}"
+
+
+@pytest.fixture(autouse=True)
+def device_status_clean():
+    _lib.device_status(0, clear=True)
+    yield
+    assert _lib.device_status(0) == 0, "a kernel recorded an error"
+
+
+def cuda(x):
+    return x.to(DEV)
+
+
+@pytest.mark.parametrize("name", ["prefill_causal_gqa", "prefill_noncausal", "prefill_causal_d128"])
+def test_prefill_matches_reference_golden(name):
+    f = load(name)
+    O = flash_attention_prefill(cuda(f["Q"]), cuda(f["K"]), cuda(f["V"]), f["causal"], f["softmax_scale"], f["group"])
+    assert O.shape == f["O"].shape and O.dtype == torch.float16
+    check_close(O, f["O"])
+    check_close(O, N.prefill_reference(f["Q"], f["K"], f["V"], f["causal"], f["softmax_scale"], f["group"]))
+
+
+def test_prefill_varlen_matches_reference_golden():
+    f = load("prefill_varlen")
+    O = flash_attention_prefill_varlen(cuda(f["Q"]), cuda(f["K"]), cuda(f["V"]), True, f["softmax_scale"],
+                                       f["group"], cuda(f["varlen"]))
+    check_close(O, f["O"])
+
+
+@pytest.mark.parametrize("causal", [True, False])
+@pytest.mark.parametrize("S", [1, 64, 100, 128, 129, 300])
+@pytest.mark.parametrize("D,G", [(64, 1), (64, 4), (128, 2), (128, 8)])
+def test_prefill_shapes(causal, S, D, G):
+    c = W.make_prefill(B=2, Hq=2 * G, Hkv=2, S=S, D=D, causal=causal, seed=S * 10 + D + G)
+    O = flash_attention_prefill(cuda(c.Q), cuda(c.K), cuda(c.V), causal, c.softmax_scale, G)
+    check_close(O, N.prefill_reference(c.Q, c.K, c.V, causal, c.softmax_scale, G))
+
+
+@pytest.mark.parametrize("D", [64, 128])
+def test_prefill_bf16(D):
+    c = W.make_prefill(B=1, Hq=4, Hkv=1, S=257, D=D, causal=True, seed=5, dtype=torch.bfloat16)
+    O = flash_attention_prefill(cuda(c.Q), cuda(c.K), cuda(c.V), True, c.softmax_scale, 4)
+    assert O.dtype == torch.bfloat16
+    check_close(O, N.prefill_reference(c.Q, c.K, c.V, True, c.softmax_scale, 4), torch.bfloat16)
+
+
+def test_causal_row_zero_is_v_row_zero_exactly():
+    c = W.make_prefill(B=2, Hq=8, Hkv=2, S=200, D=64, causal=True, seed=6)
+    O = flash_attention_prefill(cuda(c.Q), cuda(c.K), cuda(c.V), True, c.softmax_scale, 4)
+    Vx = c.V.repeat_interleave(4, dim=1)
+    assert torch.equal(O[:, :, 0].cpu(), Vx[:, :, 0])
+
+
+@pytest.mark.parametrize("causal", [True, False])
+def test_prefill_varlen_shapes(causal):
+    c = W.make_prefill(B=4, Hq=8, Hkv=2, S=384, D=64, causal=causal, seed=7)
+    lens = torch.tensor([384, 1, 129, 200], dtype=torch.int64)  # reference passes an int64 tensor
+    O = flash_attention_prefill_varlen(cuda(c.Q), cuda(c.K), cuda(c.V), causal, c.softmax_scale, 4, cuda(lens))
+    check_close(O, N.prefill_varlen_reference(c.Q, c.K, c.V, causal, c.softmax_scale, 4, lens))
+
+
+def test_prefill_strided_inputs():
+    c = W.make_prefill(B=2, Hq=4, Hkv=2, S=150, D=64, causal=True, seed=8)
+    Qt = cuda(c.Q).transpose(1, 2).contiguous().transpose(1, 2)   # [B,H,S,D] view, token-major storage
+    Kt = cuda(c.K).transpose(1, 2).contiguous().transpose(1, 2)
+    O = flash_attention_prefill(Qt, Kt, cuda(c.V), True, c.softmax_scale, 2)
+    check_close(O, N.prefill_reference(c.Q, c.K, c.V, True, c.softmax_scale, 2))
+
+
+def test_prefill_reference_asserts():
+    Q = torch.zeros(1, 4, 64, 96, dtype=torch.float16, device=DEV)
+    with pytest.raises(AssertionError):
+        flash_attention_prefill(Q, Q[:, :2], Q[:, :2], True, 0.1, 2)
+    with pytest.raises(AssertionError):
+        flash_attention_prefill(Q[..., :64], Q[:, :1, :, :64], Q[:, :1, :, :64], True, 0.1, 2)
+
+
+# ---------------------------------------------------------------- BASELINE cfg0 / cfg1, full size
+def _sampled_ref(c, heads, varlen=None):
+    B, H, S, D = c.Q.shape
+    out = {}
+    for (b, h) in heads:
+        kvh = h // c.group
+        Q = c.Q[b:b + 1, h:h + 1].cpu()
+        K = c.K[b:b + 1, kvh:kvh + 1].cpu()
+        V = c.V[b:b + 1, kvh:kvh + 1].cpu()
+        if varlen is None:
+            out[(b, h)] = N.prefill_reference(Q, K, V, c.causal, c.softmax_scale, 1)[0, 0]
+        else:
+            out[(b, h)] = N.prefill_varlen_reference(Q, K, V, c.causal, c.softmax_scale, 1, varlen[b:b + 1])[0, 0]
+    return out
+
+
+def test_prefill_cfg0_full_size_sampled():
+    c = W.make_prefill(seed=0, device=DEV)  # Q [8,64,1024,64], K/V [8,16,1024,64], causal, fp16
+    O = flash_attention_prefill(c.Q, c.K, c.V, True, c.softmax_scale, c.group)
+    assert O.shape == (8, 64, 1024, 64) and not torch.isnan(O).any()
+    heads = [(0, 0), (3, 17), (7, 63), (5, 40)]
+    for k, ref in _sampled_ref(c, heads).items():
+        check_close(O[k[0], k[1]], ref)
+
+
+def test_prefill_cfg1_varlen_full_size_sampled():
+    c = W.make_prefill(seed=1, device=DEV, varlen=True)
+    O = flash_attention_prefill_varlen(c.Q, c.K, c.V, True, c.softmax_scale, c.group, c.varlen)
+    lens = c.varlen.cpu()
+    heads = [(0, 5), (1, 33), (int(lens.argmin()), 7), (6, 62)]
+    for k, ref in _sampled_ref(c, heads, lens).items():
+        check_close(O[k[0], k[1]], ref)
+    for b in range(8):
+        assert torch.all(O[b, :, int(lens[b]):] == 0)
