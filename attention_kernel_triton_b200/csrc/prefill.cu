@@ -38,15 +38,20 @@ namespace {
 constexpr int BM = 128;            // query rows per CTA
 constexpr int BN = 128;            // keys per tile
 constexpr int kThreads = 192;
-constexpr int kTmemCols = 512;
-constexpr int kColS0 = 0, kColS1 = 128, kColO = 256;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 
+// D=64: one S buffer in TMEM (256 columns) and 112 KB of shared memory, so
+// two CTAs share an SM (two softmax warpgroups to hide each other's latency).
+// D=128: double-buffered S (512 columns), one CTA per SM.
 template <int D>
 struct Cfg {
   static constexpr int DB = D / 64;                       // 64-element (128 B) swizzle blocks per row
-  static constexpr int NSTAGE = D == 64 ? 3 : 2;          // K/V ring
-  static constexpr int NP = D == 64 ? 2 : 1;              // P buffers
+  static constexpr int NSB = D == 64 ? 1 : 2;             // S buffers in TMEM
+  static constexpr int TMEM_COLS = D == 64 ? 256 : 512;
+  static constexpr int COL_O = NSB * BN;
+  static constexpr int CTAS_PER_SM = D == 64 ? 2 : 1;
+  static constexpr int NSTAGE = 2;                        // K/V ring
+  static constexpr int NP = 1;                            // P buffers
   static constexpr uint32_t Q_BYTES = BM * D * 2;
   static constexpr uint32_t KV_BYTES = BN * D * 2;        // one of K or V
   static constexpr uint32_t P_BYTES = BM * BN * 2;
@@ -55,7 +60,7 @@ struct Cfg {
   static constexpr uint32_t OFF_V = OFF_K + NSTAGE * KV_BYTES;
   static constexpr uint32_t OFF_P = OFF_V + NSTAGE * KV_BYTES;
   static constexpr uint32_t OFF_BAR = OFF_P + NP * P_BYTES;
-  static constexpr uint32_t SMEM = OFF_BAR + 256 + 1024;  // + barriers, + alignment slack
+  static constexpr uint32_t SMEM = OFF_BAR + 256;         // + barriers (base is 1024-aligned)
 };
 
 struct PrefillParams {
@@ -147,7 +152,7 @@ __device__ __forceinline__ uint32_t pack_p(float a, float b) {
 // kernel
 // -------------------------------------------------------------------------
 template <typename T, int D>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, Cfg<D>::CTAS_PER_SM)
     prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                        const __grid_constant__ CUtensorMap tmV, const PrefillParams p) {
   using C = Cfg<D>;
@@ -155,16 +160,19 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr uint32_t IDESC_S = idesc_f16(fmt, BM, BN, 0);
   constexpr uint32_t IDESC_PV = idesc_f16(fmt, BM, D, 1);
 
-  extern __shared__ unsigned char smem_raw[];
-  unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  extern __shared__ __align__(1024) unsigned char smem[];
+  if (smem_u32(smem) & 1023u) {  // swizzled tiles need a 1024-byte aligned base
+    if (threadIdx.x == 0) record_status(kStatusWaitTimeout);
+    return;
+  }
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
   uint64_t* q_full = bars + 0;
   uint64_t* k_full = bars + 1;                   // [NSTAGE]
   uint64_t* v_full = k_full + C::NSTAGE;         // [NSTAGE]
   uint64_t* kv_empty = v_full + C::NSTAGE;       // [NSTAGE]
-  uint64_t* s_full = kv_empty + C::NSTAGE;       // [2]
-  uint64_t* s_empty = s_full + 2;                // [2]
-  uint64_t* p_full = s_empty + 2;                // [NP]
+  uint64_t* s_full = kv_empty + C::NSTAGE;       // [NSB]
+  uint64_t* s_empty = s_full + C::NSB;           // [NSB]
+  uint64_t* p_full = s_empty + C::NSB;           // [NP]
   uint64_t* p_empty = p_full + C::NP;            // [NP]
   uint64_t* o_done = p_empty + C::NP;            // 1
   uint64_t* mma_idle = o_done + 1;               // 1
@@ -197,7 +205,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&v_full[s], 1);
       mbar_init(&kv_empty[s], 1);
     }
-    for (int s = 0; s < 2; ++s) {
+    for (int s = 0; s < C::NSB; ++s) {
       mbar_init(&s_full[s], 1);
       mbar_init(&s_empty[s], 4);
     }
@@ -212,7 +220,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   if (warp == 5) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                 "r"(kTmemCols));
+                 "r"(C::TMEM_COLS));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   tc_fence_before();
@@ -264,16 +272,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       for (int j = 0; ok && j <= n_kv; ++j) {
         if (j < n_kv) {
-          const int st = j % C::NSTAGE, sb = j & 1;
+          const int st = j % C::NSTAGE, sb = j % C::NSB;
           if (!wait(&k_full[st], (j / C::NSTAGE) & 1)) break;
-          if (j >= 2 && !wait(&s_empty[sb], ((j >> 1) - 1) & 1)) break;
+          if (j >= C::NSB && !wait(&s_empty[sb], ((j / C::NSB) - 1) & 1)) break;
           tc_fence_after();
           const uint32_t sK = smem_u32(smem + C::OFF_K + st * C::KV_BYTES);
 #pragma unroll
           for (int k = 0; k < D / 16; ++k) {
             const uint32_t off = (k >> 2) * (BM * 128) + (k & 3) * 32;
             const uint32_t offk = (k >> 2) * (BN * 128) + (k & 3) * 32;
-            mma_f16(tmem + (sb ? kColS1 : kColS0), desc_sw128(sQ + off, 16, 1024), desc_sw128(sK + offk, 16, 1024),
+            mma_f16(tmem + sb * BN, desc_sw128(sQ + off, 16, 1024), desc_sw128(sK + offk, 16, 1024),
                     IDESC_S, k > 0);
           }
           mma_commit(&s_full[sb]);
@@ -288,7 +296,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int k = 0; k < BN / 16; ++k) {
             const uint32_t offp = (k >> 2) * (BM * 128) + (k & 3) * 32;
-            mma_f16(tmem + kColO, desc_sw128(sP + offp, 16, 1024), desc_sw128(sV + k * 2048, BN * 128, 1024),
+            mma_f16(tmem + C::COL_O, desc_sw128(sP + offp, 16, 1024), desc_sw128(sV + k * 2048, BN * 128, 1024),
                     IDESC_PV, (i > 0 || k > 0) ? 1u : 0u);
           }
           mma_commit(o_done);
@@ -309,31 +317,37 @@ __global__ void __launch_bounds__(kThreads, 1)
     int pv_seen = 0;
     bool ok = true;
     for (int j = 0; j < n_kv; ++j) {
-      const int sb = j & 1, pb = j % C::NP;
-      if (!wait(&s_full[sb], (j >> 1) & 1)) { ok = false; break; }
+      const int sb = j % C::NSB, pb = j % C::NP;
+      if (!wait(&s_full[sb], (j / C::NSB) & 1)) { ok = false; break; }
       tc_fence_after();
       float x[BN];
+      {
+        uint32_t r[BN / 32][32];
 #pragma unroll
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld32(tmem + lane_addr + (sb ? kColS1 : kColS0) + c * 32, r);
+        for (int c = 0; c < BN / 32; ++c) tmem_ld32(tmem + lane_addr + sb * BN + c * 32, r[c]);
         tmem_wait_ld();
 #pragma unroll
-        for (int e = 0; e < 32; ++e) x[c * 32 + e] = __uint_as_float(r[e]);
+        for (int c = 0; c < BN / 32; ++c)
+#pragma unroll
+          for (int e = 0; e < 32; ++e) x[c * 32 + e] = __uint_as_float(r[c][e]);
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&s_empty[sb]);
-      // scale, mask, row max
-      const int col0 = j * BN;
-      float mx = -INFINITY;
+      // masks only on the last key tile (causal diagonal, keys past S)
+      if (j == n_kv - 1) {
+        const int lim = min(p.causal ? row : p.S - 1, p.S - 1) - j * BN;  // last visible column
 #pragma unroll
-      for (int c = 0; c < BN; ++c) {
-        const int col = col0 + c;
-        const bool masked = (p.causal && col > row) || col >= p.S;
-        x[c] = masked ? -INFINITY : x[c] * p.scale_log2;
-        mx = fmaxf(mx, x[c]);
+        for (int c = 0; c < BN; ++c) x[c] = c > lim ? -INFINITY : x[c];
       }
+      // row max of the raw scores (scale > 0), 8 independent chains
+      float mx8[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) mx8[e] = x[e];
+#pragma unroll
+      for (int c = 8; c < BN; ++c) mx8[c & 7] = fmaxf(mx8[c & 7], x[c]);
+      const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                             fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7]))) * p.scale_log2;
       const float m_new = fmaxf(m_use, mx);
       const bool need = m_new > m_use + kRescaleThreshold || (m_use == -INFINITY && m_new != -INFINITY);
       float alpha = 1.f;
@@ -342,17 +356,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         m_use = m_new;
       }
       const float m_sub = m_use == -INFINITY ? 0.f : m_use;
-      // P = 2^(x - m) in the input dtype, into the swizzled K-major P tile
+      // P = 2^(s*scale - m) in the input dtype, into the swizzled K-major P tile
       if (j >= C::NP && !wait(&p_empty[pb], ((j / C::NP) - 1) & 1)) { ok = false; break; }
       unsigned char* sP = smem + C::OFF_P + pb * C::P_BYTES;
-      float rs = 0.f;
+      float rs8[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) rs8[e] = 0.f;
 #pragma unroll
       for (int ch = 0; ch < BN / 8; ++ch) {
         float pv[8];
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
-          pv[e] = fast_exp2(x[ch * 8 + e] - m_sub);
-          rs += pv[e];
+          pv[e] = fast_exp2(fmaf(x[ch * 8 + e], p.scale_log2, -m_sub));
+          rs8[e] += pv[e];
         }
         uint4 w;
         w.x = pack_p<T>(pv[0], pv[1]);
@@ -362,6 +378,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int kb = ch >> 3, cin = ch & 7;
         *reinterpret_cast<uint4*>(sP + kb * (BM * 128) + t * 128 + ((cin ^ (t & 7)) << 4)) = w;
       }
+      const float rs = ((rs8[0] + rs8[1]) + (rs8[2] + rs8[3])) + ((rs8[4] + rs8[5]) + (rs8[6] + rs8[7]));
       l = l * alpha + rs;
       // O must see PV_{j-1} finished before it is rescaled or before PV_j is queued
       if (j >= 1) {
@@ -375,11 +392,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int c = 0; c < D / 32; ++c) {
             uint32_t r[32];
-            tmem_ld32(tmem + lane_addr + kColO + c * 32, r);
+            tmem_ld32(tmem + lane_addr + C::COL_O + c * 32, r);
             tmem_wait_ld();
 #pragma unroll
             for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * alpha);
-            tmem_st32(tmem + lane_addr + kColO + c * 32, r);
+            tmem_st32(tmem + lane_addr + C::COL_O + c * 32, r);
           }
           tmem_wait_st();
         }
@@ -402,7 +419,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
     for (int c = 0; c < D / 32; ++c) {
       uint32_t r[32];
-      tmem_ld32(tmem + lane_addr + kColO + c * 32, r);
+      tmem_ld32(tmem + lane_addr + C::COL_O + c * 32, r);
       tmem_wait_ld();
       if (row < p.S) {
 #pragma unroll
@@ -421,7 +438,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   if (warp == 5) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(C::TMEM_COLS));
   }
 }
 
@@ -497,6 +514,8 @@ extern "C" int akt_prefill(const akt_prefill_args* a, void* stream) {
     if (s % 8) return set_error(AKT_ERR_UNSUPPORTED, "prefill: strides must be multiples of 16 bytes");
   if (!al16(a->q) || !al16(a->k) || !al16(a->v) || !al16(a->out))
     return set_error(AKT_ERR_UNSUPPORTED, "prefill: 16-byte alignment required");
+  if (!(a->softmax_scale > 0.f) || a->softmax_scale == INFINITY)
+    return set_error(AKT_ERR_UNSUPPORTED, "prefill: softmax_scale must be positive and finite");
   if (a->batch == 0 || a->seq_len == 0) return AKT_OK;
   CUtensorMap mq, mk, mv;
   int rc = make_map(&mq, a->q, a->dtype, a->batch, a->num_qo_heads, a->seq_len, a->head_dim, a->q_stride_batch,

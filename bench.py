@@ -143,6 +143,83 @@ def run_reference(args):
     }), flush=True)
 
 
+def measured_tflops():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            return float(json.load(f)["bf16_tflops"]), "measured"
+    return 1590.0, "fallback"
+
+
+def time_kernels(fn, iters, dev, flush=None):
+    """Mean device time (ms) of the library's main kernel over ``iters`` calls,
+    from CUDA events the library records around that kernel on its stream.
+    ``flush`` (a buffer larger than L2) is overwritten before every call."""
+    from attention_kernel_triton_b200 import _lib
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize(dev)
+    with _lib.profile_kernels() as prof:
+        for _ in range(iters):
+            if flush is not None:
+                flush.zero_()
+            fn()
+        torch.cuda.synchronize(dev)
+    return prof.total_ms / max(prof.launches, 1)
+
+
+def secondary_measurements(dev, iters=20):
+    """The other BASELINE configurations, one kernel each (single GPU)."""
+    from attention_kernel_triton_b200.decode_flash_attention_redundant import flash_attention_decode
+    from attention_kernel_triton_b200.magicpig_sparsetoken_decode_flash_attention_redundant_var_len_paged_with_norm import (
+        magicpig_sparsetoken_flash_attention_decode_paged)
+    from attention_kernel_triton_b200.prefill_flash_attention import flash_attention_prefill
+    from attention_kernel_triton_b200.prefill_flash_attention_var_len_padding import (
+        flash_attention_prefill as flash_attention_prefill_varlen)
+    from attention_kernel_triton_b200.sparsetoken_decode_flash_attention_redundant import (
+        sparsetoken_flash_attention_decode)
+    from attention_kernel_triton_b200.sparsetoken_decode_flash_attention_redundant_var_len_paged import (
+        sparsetoken_flash_attention_decode_paged)
+    hbm, _ = measured_peaks()
+    tf, _ = measured_tflops()
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)  # 256 MB > 126 MB L2
+    out = {}
+
+    c = W.make_prefill(seed=0, device=dev)
+    ms = time_kernels(lambda: flash_attention_prefill(c.Q, c.K, c.V, True, c.softmax_scale, c.group), iters, dev,
+                      flush)
+    out["prefill_cfg0_causal"] = {"tflops": c.flops / ms / 1e9, "ms": ms, "frac_of_bf16_peak": c.flops / ms / 1e9 / tf,
+                                  "gflop": c.flops / 1e9, "l2": "flushed"}
+    c = W.make_prefill(seed=1, device=dev, varlen=True)
+    ms = time_kernels(lambda: flash_attention_prefill_varlen(c.Q, c.K, c.V, True, c.softmax_scale, c.group,
+                                                             c.varlen), iters, dev, flush)
+    out["prefill_cfg1_varlen"] = {"tflops": c.flops / ms / 1e9, "ms": ms, "frac_of_bf16_peak": c.flops / ms / 1e9 / tf,
+                                  "gflop_valid": c.flops / 1e9, "lens": c.varlen.tolist(), "l2": "flushed"}
+    del c
+    for name, kw, fl in [("decode_cfg2", dict(B=8, Hq=64, Hkv=16, L=1024, D=64), True),
+                         ("decode_L4K", dict(B=1, Hq=32, Hkv=8, L=4096, D=128), True),
+                         ("decode_L32K", dict(B=1, Hq=32, Hkv=8, L=32768, D=128), True),
+                         ("decode_L128K", dict(B=1, Hq=32, Hkv=8, L=131072, D=128), False)]:
+        d = W.make_decode(seed=2, device=dev, **kw)
+        ms = time_kernels(lambda: flash_attention_decode(d.q, d.K, d.V, d.softmax_scale, d.group), iters, dev,
+                          flush if fl else None)
+        out[name] = {"gbs": d.bytes / ms / 1e6, "ms": ms, "frac_of_hbm": d.bytes / ms / 1e6 / hbm,
+                     "mb": d.bytes / 1e6, "l2": "flushed" if fl else "inputs larger than L2"}
+    sd = W.make_sparse_dense(seed=41, device=dev)
+    ms = time_kernels(lambda: sparsetoken_flash_attention_decode(sd.q, sd.K, sd.V, sd.sparse_ind, sd.sparse_nnz,
+                                                                 sd.softmax_scale, sd.group), iters, dev, flush)
+    out["sparse_cfg4_dense"] = {"gbs": sd.bytes / ms / 1e6, "ms": ms, "mb": sd.bytes / 1e6, "l2": "flushed"}
+    del sd
+    sp = W.make_sparse_paged(seed=42, device=dev, magicpig=True)
+    ms = time_kernels(lambda: sparsetoken_flash_attention_decode_paged(sp.q, sp.cache, sp.indptr, sp.indices,
+                                                                       sp.sparse_ind, sp.sparse_nnz), iters, dev, flush)
+    out["sparse_cfg4_paged"] = {"gbs": sp.bytes / ms / 1e6, "ms": ms, "mb": sp.bytes / 1e6, "l2": "flushed"}
+    ms = time_kernels(lambda: magicpig_sparsetoken_flash_attention_decode_paged(
+        sp.q, sp.cache, sp.indptr, sp.indices, sp.sparse_ind, sp.sparse_nnz, sp.K, sp.L), iters, dev, flush)
+    out["magicpig_cfg4_paged"] = {"gbs": sp.bytes / ms / 1e6, "ms": ms, "mb": sp.bytes / 1e6, "l2": "flushed"}
+    return out
+
+
 def run_ours(args):
     from attention_kernel_triton_b200 import _lib
     from attention_kernel_triton_b200.decode_flash_attention_redundant_var_len_paged import (
@@ -236,6 +313,11 @@ def run_ours(args):
     peak, peak_kind = measured_peaks()
     achieved = nbytes / (kern_ms * 1e-3) / 1e9
     result = None
+    secondary = None
+    if world == 1 and not args.no_secondary:
+        del c
+        torch.cuda.empty_cache()
+        secondary = secondary_measurements(dev)
     if rank == 0:
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
@@ -265,6 +347,8 @@ def run_ours(args):
             "gpu_launches": 3 * args.steps,
             "clocks": clk,
         }
+        if secondary is not None:
+            result["secondary"] = secondary
         print(json.dumps(result), flush=True)
     if pg is not None:
         pg.barrier()
@@ -281,6 +365,8 @@ def main():
     ap.add_argument("--batch", type=int, default=64,
                     help="sequences per GPU (64 = cfg3; smaller only for profiler captures)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-secondary", action="store_true",
+                    help="skip the other configurations (prefill, dense decode, sparse)")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)
