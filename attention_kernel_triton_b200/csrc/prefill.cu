@@ -26,6 +26,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <cstdlib>
 #include <mutex>
 #include <string>
 
@@ -36,31 +37,46 @@ int set_error(int code, const std::string& msg);
 namespace {
 
 constexpr int BM = 128;            // query rows per CTA
-constexpr int BN = 128;            // keys per tile
 constexpr int kThreads = 192;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 
-// D=64: one S buffer in TMEM (256 columns) and 112 KB of shared memory, so
-// two CTAs share an SM (two softmax warpgroups to hide each other's latency).
-// D=128: double-buffered S (512 columns), one CTA per SM.
-template <int D>
+__host__ __device__ constexpr int pow2_at_least(int x) {
+  int v = 32;
+  while (v < x) v *= 2;
+  return v;
+}
+
+// Tile configuration per (head_dim D, keys per tile BN).  TMEM holds S
+// (NSB buffers of BN fp32 columns) and O (D columns); shared memory holds Q,
+// a two-stage K/V ring and one P tile.  Smaller footprints let more CTAs (and
+// so more softmax warpgroups) share an SM:
+//   D=64,  BN=64 : TMEM 128 cols,  64 KB smem -> 3 CTAs/SM
+//   D=64,  BN=128: TMEM 256 cols, 112 KB smem -> 2 CTAs/SM
+//   D=128, BN=64 : TMEM 256 cols, 112 KB smem -> 2 CTAs/SM
+//   D=128, BN=128: TMEM 512 cols (S double-buffered), 192 KB -> 1 CTA/SM
+template <int D, int BN_>
 struct Cfg {
+  static constexpr int BN = BN_;
   static constexpr int DB = D / 64;                       // 64-element (128 B) swizzle blocks per row
-  static constexpr int NSB = D == 64 ? 1 : 2;             // S buffers in TMEM
-  static constexpr int TMEM_COLS = D == 64 ? 256 : 512;
+  static constexpr int NSB = (D == 128 && BN == 128) ? 2 : 1;
   static constexpr int COL_O = NSB * BN;
-  static constexpr int CTAS_PER_SM = D == 64 ? 2 : 1;
-  static constexpr int NSTAGE = 2;                        // K/V ring
+  static constexpr int TMEM_COLS = pow2_at_least(COL_O + D);
+  // K and V rings are separate: a K stage is released when its S MMA is done,
+  // a V stage when its P.V MMA is done, so K loads run further ahead.
+  static constexpr int NSK = (D == 64 && BN == 64) ? 3 : 2;
+  static constexpr int NSV = 2;
   static constexpr int NP = 1;                            // P buffers
   static constexpr uint32_t Q_BYTES = BM * D * 2;
-  static constexpr uint32_t KV_BYTES = BN * D * 2;        // one of K or V
+  static constexpr uint32_t KV_BYTES = BN * D * 2;        // one K or V tile
   static constexpr uint32_t P_BYTES = BM * BN * 2;
   static constexpr uint32_t OFF_Q = 0;
   static constexpr uint32_t OFF_K = OFF_Q + Q_BYTES;
-  static constexpr uint32_t OFF_V = OFF_K + NSTAGE * KV_BYTES;
-  static constexpr uint32_t OFF_P = OFF_V + NSTAGE * KV_BYTES;
+  static constexpr uint32_t OFF_V = OFF_K + NSK * KV_BYTES;
+  static constexpr uint32_t OFF_P = OFF_V + NSV * KV_BYTES;
   static constexpr uint32_t OFF_BAR = OFF_P + NP * P_BYTES;
   static constexpr uint32_t SMEM = OFF_BAR + 256;         // + barriers (base is 1024-aligned)
+  static constexpr int CTAS_PER_SM = (SMEM + 1024) * 3 <= 228 * 1024 && TMEM_COLS * 3 <= 512 ? 3
+                                     : (SMEM + 1024) * 2 <= 228 * 1024 && TMEM_COLS * 2 <= 512 ? 2 : 1;
 };
 
 struct PrefillParams {
@@ -143,6 +159,18 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, i
       : "memory");
 }
 
+// one lane of a converged warp (the issuing lane for MMA / TMA / commit)
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred = 0;
+  asm volatile(
+      "{\n\t.reg .b32 rx;\n\t.reg .pred px;\n\t"
+      "elect.sync rx|px, %1;\n\t"
+      "@px mov.s32 %0, 1;\n\t}"
+      : "+r"(pred)
+      : "r"(0xffffffffu));
+  return pred != 0;
+}
+
 template <typename T>
 __device__ __forceinline__ uint32_t pack_p(float a, float b) {
   return Elem<T>::pack2(a, b);
@@ -151,11 +179,11 @@ __device__ __forceinline__ uint32_t pack_p(float a, float b) {
 // -------------------------------------------------------------------------
 // kernel
 // -------------------------------------------------------------------------
-template <typename T, int D>
-__global__ void __launch_bounds__(kThreads, Cfg<D>::CTAS_PER_SM)
+template <typename T, int D, int BN>
+__global__ void __launch_bounds__(kThreads, (Cfg<D, BN>::CTAS_PER_SM))
     prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                        const __grid_constant__ CUtensorMap tmV, const PrefillParams p) {
-  using C = Cfg<D>;
+  using C = Cfg<D, BN>;
   constexpr int fmt = std::is_same<T, __half>::value ? 0 : 1;
   constexpr uint32_t IDESC_S = idesc_f16(fmt, BM, BN, 0);
   constexpr uint32_t IDESC_PV = idesc_f16(fmt, BM, D, 1);
@@ -167,10 +195,11 @@ __global__ void __launch_bounds__(kThreads, Cfg<D>::CTAS_PER_SM)
   }
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
   uint64_t* q_full = bars + 0;
-  uint64_t* k_full = bars + 1;                   // [NSTAGE]
-  uint64_t* v_full = k_full + C::NSTAGE;         // [NSTAGE]
-  uint64_t* kv_empty = v_full + C::NSTAGE;       // [NSTAGE]
-  uint64_t* s_full = kv_empty + C::NSTAGE;       // [NSB]
+  uint64_t* k_full = bars + 1;                   // [NSK]
+  uint64_t* k_empty = k_full + C::NSK;           // [NSK]
+  uint64_t* v_full = k_empty + C::NSK;           // [NSV]
+  uint64_t* v_empty = v_full + C::NSV;           // [NSV]
+  uint64_t* s_full = v_empty + C::NSV;           // [NSB]
   uint64_t* s_empty = s_full + C::NSB;           // [NSB]
   uint64_t* p_full = s_empty + C::NSB;           // [NP]
   uint64_t* p_empty = p_full + C::NP;            // [NP]
@@ -200,10 +229,13 @@ __global__ void __launch_bounds__(kThreads, Cfg<D>::CTAS_PER_SM)
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int s = 0; s < C::NSTAGE; ++s) {
+    for (int s = 0; s < C::NSK; ++s) {
       mbar_init(&k_full[s], 1);
+      mbar_init(&k_empty[s], 1);
+    }
+    for (int s = 0; s < C::NSV; ++s) {
       mbar_init(&v_full[s], 1);
-      mbar_init(&kv_empty[s], 1);
+      mbar_init(&v_empty[s], 1);
     }
     for (int s = 0; s < C::NSB; ++s) {
       mbar_init(&s_full[s], 1);
@@ -234,9 +266,14 @@ __global__ void __launch_bounds__(kThreads, Cfg<D>::CTAS_PER_SM)
     *abort_flag = 1;
     return false;
   };
+  // warp-uniform variant for the warp that issues MMAs in lockstep
+  auto wwait = [&](uint64_t* bar, uint32_t parity) -> bool {
+    return __all_sync(0xffffffffu, wait(bar, parity)) != 0;
+  };
 
   if (warp == 4) {
-    // ========================= TMA producer =========================
+    // ========================= TMA producers =========================
+    // lane 0: Q, then the K ring; lane 1: the V ring (independent waits)
     if (lane == 0) {
       unsigned char* sQ = smem + C::OFF_Q;
       mbar_arrive_expect_tx(q_full, C::Q_BYTES);
@@ -244,70 +281,87 @@ __global__ void __launch_bounds__(kThreads, Cfg<D>::CTAS_PER_SM)
       for (int db = 0; db < C::DB; ++db) tma_load_4d(sQ + db * BM * 128, &tmQ, db * 64, q0, h, b, q_full);
       int issued = 0;
       for (int j = 0; j < n_kv; ++j) {
-        const int st = j % C::NSTAGE;
-        if (j >= C::NSTAGE && !wait(&kv_empty[st], ((j / C::NSTAGE) - 1) & 1)) break;
+        const int st = j % C::NSK;
+        if (j >= C::NSK && !wait(&k_empty[st], ((j / C::NSK) - 1) & 1)) break;
         unsigned char* sK = smem + C::OFF_K + st * C::KV_BYTES;
-        unsigned char* sV = smem + C::OFF_V + st * C::KV_BYTES;
         mbar_arrive_expect_tx(&k_full[st], C::KV_BYTES);
 #pragma unroll
         for (int db = 0; db < C::DB; ++db) tma_load_4d(sK + db * BN * 128, &tmK, db * 64, j * BN, kvh, b, &k_full[st]);
+        issued = j + 1;
+      }
+      if (*abort_flag) {  // drain loads still in flight into this CTA's shared memory
+        mbar_wait(q_full, 0);
+        for (int j = max(0, issued - C::NSK); j < issued; ++j) mbar_wait(&k_full[j % C::NSK], (j / C::NSK) & 1);
+      }
+    } else if (lane == 1) {
+      int issued = 0;
+      for (int j = 0; j < n_kv; ++j) {
+        const int st = j % C::NSV;
+        if (j >= C::NSV && !wait(&v_empty[st], ((j / C::NSV) - 1) & 1)) break;
+        unsigned char* sV = smem + C::OFF_V + st * C::KV_BYTES;
         mbar_arrive_expect_tx(&v_full[st], C::KV_BYTES);
 #pragma unroll
         for (int db = 0; db < C::DB; ++db) tma_load_4d(sV + db * BN * 128, &tmV, db * 64, j * BN, kvh, b, &v_full[st]);
         issued = j + 1;
       }
-      if (*abort_flag) {  // drain loads still in flight into this CTA's shared memory
-        mbar_wait(q_full, 0);
-        for (int j = max(0, issued - C::NSTAGE); j < issued; ++j) {
-          mbar_wait(&k_full[j % C::NSTAGE], (j / C::NSTAGE) & 1);
-          mbar_wait(&v_full[j % C::NSTAGE], (j / C::NSTAGE) & 1);
-        }
+      if (*abort_flag) {
+        for (int j = max(0, issued - C::NSV); j < issued; ++j) mbar_wait(&v_full[j % C::NSV], (j / C::NSV) & 1);
       }
     }
   } else if (warp == 5) {
     // ========================= MMA issuer =========================
-    if (lane == 0) {
-      const uint32_t sQ = smem_u32(smem + C::OFF_Q);
-      bool ok = wait(q_full, 0);
-      tc_fence_after();
-      for (int j = 0; ok && j <= n_kv; ++j) {
-        if (j < n_kv) {
-          const int st = j % C::NSTAGE, sb = j % C::NSB;
-          if (!wait(&k_full[st], (j / C::NSTAGE) & 1)) break;
-          if (j >= C::NSB && !wait(&s_empty[sb], ((j / C::NSB) - 1) & 1)) break;
-          tc_fence_after();
-          const uint32_t sK = smem_u32(smem + C::OFF_K + st * C::KV_BYTES);
+    // The whole warp runs the loop (descriptors stay warp-uniform); one
+    // elected lane issues each MMA and commit.
+    const uint32_t sQ = smem_u32(smem + C::OFF_Q);
+    bool ok = wwait(q_full, 0);
+    tc_fence_after();
+    for (int j = 0; ok && j <= n_kv; ++j) {
+      if (j < n_kv) {
+        const int st = j % C::NSK, sb = j % C::NSB;
+        if (!wwait(&k_full[st], (j / C::NSK) & 1)) break;
+        if (j >= C::NSB && !wwait(&s_empty[sb], ((j / C::NSB) - 1) & 1)) break;
+        tc_fence_after();
+        const uint32_t sK = smem_u32(smem + C::OFF_K + st * C::KV_BYTES);
+        const bool leader = elect_one();
 #pragma unroll
-          for (int k = 0; k < D / 16; ++k) {
-            const uint32_t off = (k >> 2) * (BM * 128) + (k & 3) * 32;
-            const uint32_t offk = (k >> 2) * (BN * 128) + (k & 3) * 32;
-            mma_f16(tmem + sb * BN, desc_sw128(sQ + off, 16, 1024), desc_sw128(sK + offk, 16, 1024),
-                    IDESC_S, k > 0);
-          }
-          mma_commit(&s_full[sb]);
+        for (int k = 0; k < D / 16; ++k) {
+          const uint32_t off = (k >> 2) * (BM * 128) + (k & 3) * 32;
+          const uint32_t offk = (k >> 2) * (BN * 128) + (k & 3) * 32;
+          const uint64_t da = desc_sw128(sQ + off, 16, 1024), db = desc_sw128(sK + offk, 16, 1024);
+          if (leader) mma_f16(tmem + sb * BN, da, db, IDESC_S, k > 0);
         }
-        if (j >= 1) {
-          const int i = j - 1, pb = i % C::NP, st = i % C::NSTAGE;
-          if (!wait(&p_full[pb], (i / C::NP) & 1)) break;
-          if (!wait(&v_full[st], (i / C::NSTAGE) & 1)) break;
-          tc_fence_after();
-          const uint32_t sP = smem_u32(smem + C::OFF_P + pb * C::P_BYTES);
-          const uint32_t sV = smem_u32(smem + C::OFF_V + st * C::KV_BYTES);
+        if (leader) {
+          mma_commit(&s_full[sb]);
+          mma_commit(&k_empty[st]);
+        }
+        __syncwarp();
+      }
+      if (j >= 1) {
+        const int i = j - 1, pb = i % C::NP, st = i % C::NSV;
+        if (!wwait(&p_full[pb], (i / C::NP) & 1)) break;
+        if (!wwait(&v_full[st], (i / C::NSV) & 1)) break;
+        tc_fence_after();
+        const uint32_t sP = smem_u32(smem + C::OFF_P + pb * C::P_BYTES);
+        const uint32_t sV = smem_u32(smem + C::OFF_V + st * C::KV_BYTES);
+        const bool leader = elect_one();
 #pragma unroll
-          for (int k = 0; k < BN / 16; ++k) {
-            const uint32_t offp = (k >> 2) * (BM * 128) + (k & 3) * 32;
-            mma_f16(tmem + C::COL_O, desc_sw128(sP + offp, 16, 1024), desc_sw128(sV + k * 2048, BN * 128, 1024),
-                    IDESC_PV, (i > 0 || k > 0) ? 1u : 0u);
-          }
+        for (int k = 0; k < BN / 16; ++k) {
+          const uint32_t offp = (k >> 2) * (BM * 128) + (k & 3) * 32;
+          const uint64_t da = desc_sw128(sP + offp, 16, 1024), db = desc_sw128(sV + k * 2048, BN * 128, 1024);
+          if (leader) mma_f16(tmem + C::COL_O, da, db, IDESC_PV, (i > 0 || k > 0) ? 1u : 0u);
+        }
+        if (leader) {
           mma_commit(o_done);
           mma_commit(&p_empty[pb]);
-          mma_commit(&kv_empty[st]);
+          mma_commit(&v_empty[st]);
         }
+        __syncwarp();
       }
-      // every MMA issued by this thread has finished before the CTA can exit
-      mma_commit(mma_idle);
-      mbar_wait(mma_idle, 0);
     }
+    // every MMA issued by this warp has finished before the CTA can exit
+    if (elect_one()) mma_commit(mma_idle);
+    __syncwarp();
+    mbar_wait(mma_idle, 0);
   } else {
     // ========================= softmax warpgroup =========================
     const int t = threadIdx.x;  // 0..127: row t of the tile, TMEM lane t
@@ -334,8 +388,9 @@ __global__ void __launch_bounds__(kThreads, Cfg<D>::CTAS_PER_SM)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&s_empty[sb]);
-      // masks only on the last key tile (causal diagonal, keys past S)
-      if (j == n_kv - 1) {
+      // masks only where a key tile reaches past the tile's first row (causal
+      // diagonal) or past S
+      if ((p.causal && (j + 1) * BN - 1 > q0) || (j + 1) * BN > p.S) {
         const int lim = min(p.causal ? row : p.S - 1, p.S - 1) - j * BN;  // last visible column
 #pragma unroll
         for (int c = 0; c < BN; ++c) x[c] = c > lim ? -INFINITY : x[c];
@@ -356,12 +411,12 @@ __global__ void __launch_bounds__(kThreads, Cfg<D>::CTAS_PER_SM)
         m_use = m_new;
       }
       const float m_sub = m_use == -INFINITY ? 0.f : m_use;
-      // P = 2^(s*scale - m) in the input dtype, into the swizzled K-major P tile
-      if (j >= C::NP && !wait(&p_empty[pb], ((j / C::NP) - 1) & 1)) { ok = false; break; }
-      unsigned char* sP = smem + C::OFF_P + pb * C::P_BYTES;
+      // P = 2^(s*scale - m) in the input dtype, packed in registers first so the
+      // exponentials do not wait for the previous P.V to release the P tile
       float rs8[8];
 #pragma unroll
       for (int e = 0; e < 8; ++e) rs8[e] = 0.f;
+      uint32_t pk[BN / 2];
 #pragma unroll
       for (int ch = 0; ch < BN / 8; ++ch) {
         float pv[8];
@@ -370,13 +425,16 @@ __global__ void __launch_bounds__(kThreads, Cfg<D>::CTAS_PER_SM)
           pv[e] = fast_exp2(fmaf(x[ch * 8 + e], p.scale_log2, -m_sub));
           rs8[e] += pv[e];
         }
-        uint4 w;
-        w.x = pack_p<T>(pv[0], pv[1]);
-        w.y = pack_p<T>(pv[2], pv[3]);
-        w.z = pack_p<T>(pv[4], pv[5]);
-        w.w = pack_p<T>(pv[6], pv[7]);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) pk[ch * 4 + e] = pack_p<T>(pv[2 * e], pv[2 * e + 1]);
+      }
+      if (j >= C::NP && !wait(&p_empty[pb], ((j / C::NP) - 1) & 1)) { ok = false; break; }
+      unsigned char* sP = smem + C::OFF_P + pb * C::P_BYTES;
+#pragma unroll
+      for (int ch = 0; ch < BN / 8; ++ch) {
         const int kb = ch >> 3, cin = ch & 7;
-        *reinterpret_cast<uint4*>(sP + kb * (BM * 128) + t * 128 + ((cin ^ (t & 7)) << 4)) = w;
+        *reinterpret_cast<uint4*>(sP + kb * (BM * 128) + t * 128 + ((cin ^ (t & 7)) << 4)) =
+            make_uint4(pk[ch * 4 + 0], pk[ch * 4 + 1], pk[ch * 4 + 2], pk[ch * 4 + 3]);
       }
       const float rs = ((rs8[0] + rs8[1]) + (rs8[2] + rs8[3])) + ((rs8[4] + rs8[5]) + (rs8[6] + rs8[7]));
       l = l * alpha + rs;
@@ -460,12 +518,12 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 
 // 4-D map over [B][H][S][D] (element strides sb, sh, ss; dim stride 1), box 64 x 128
 int make_map(CUtensorMap* m, const void* base, int dtype, int B, int H, int S, int D, int64_t sb, int64_t sh,
-             int64_t ss) {
+             int64_t ss, int box_rows) {
   auto fn = encode_fn();
   if (!fn) return set_error(AKT_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
   cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)S, (cuuint64_t)H, (cuuint64_t)B};
   cuuint64_t strides[3] = {(cuuint64_t)ss * 2, (cuuint64_t)sh * 2, (cuuint64_t)sb * 2};
-  cuuint32_t box[4] = {64, 128, 1, 1};
+  cuuint32_t box[4] = {64, (cuuint32_t)box_rows, 1, 1};
   cuuint32_t estr[4] = {1, 1, 1, 1};
   CUresult r = fn(m, dtype == AKT_FLOAT16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4,
                   const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
@@ -474,11 +532,11 @@ int make_map(CUtensorMap* m, const void* base, int dtype, int B, int H, int S, i
   return AKT_OK;
 }
 
-template <typename T, int D>
+template <typename T, int D, int BN>
 int launch_prefill(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const PrefillParams& p,
                    cudaStream_t st) {
-  auto kern = prefill_fwd_kernel<T, D>;
-  const int smem = (int)Cfg<D>::SMEM;
+  auto kern = prefill_fwd_kernel<T, D, BN>;
+  const int smem = (int)Cfg<D, BN>::SMEM;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return set_error(AKT_ERR_CUDA, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
   dim3 grid(p.n_q_tiles, p.Hq, p.B);
@@ -492,6 +550,18 @@ int launch_prefill(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorM
 }
 
 bool al16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; }
+
+// keys per tile: AKT_PREFILL_BN (64 or 128) overrides the default, read once
+int prefill_key_tile(int D) {
+  static int forced = -1;
+  if (forced < 0) {
+    const char* v = getenv("AKT_PREFILL_BN");
+    forced = v ? atoi(v) : 0;
+    if (forced != 64 && forced != 128) forced = 0;
+  }
+  if (forced) return forced;
+  return D == 64 ? 64 : 128;
+}
 
 }  // namespace
 }  // namespace akt
@@ -517,13 +587,14 @@ extern "C" int akt_prefill(const akt_prefill_args* a, void* stream) {
   if (!(a->softmax_scale > 0.f) || a->softmax_scale == INFINITY)
     return set_error(AKT_ERR_UNSUPPORTED, "prefill: softmax_scale must be positive and finite");
   if (a->batch == 0 || a->seq_len == 0) return AKT_OK;
+  const int bn = prefill_key_tile(a->head_dim);
   CUtensorMap mq, mk, mv;
   int rc = make_map(&mq, a->q, a->dtype, a->batch, a->num_qo_heads, a->seq_len, a->head_dim, a->q_stride_batch,
-                    a->q_stride_head, a->q_stride_token);
+                    a->q_stride_head, a->q_stride_token, BM);
   if (!rc) rc = make_map(&mk, a->k, a->dtype, a->batch, a->num_kv_heads, a->seq_len, a->head_dim, a->k_stride_batch,
-                         a->k_stride_head, a->k_stride_token);
+                         a->k_stride_head, a->k_stride_token, bn);
   if (!rc) rc = make_map(&mv, a->v, a->dtype, a->batch, a->num_kv_heads, a->seq_len, a->head_dim, a->v_stride_batch,
-                         a->v_stride_head, a->v_stride_token);
+                         a->v_stride_head, a->v_stride_token, bn);
   if (rc) return rc;
   PrefillParams p{};
   p.o = a->out;
@@ -536,9 +607,13 @@ extern "C" int akt_prefill(const akt_prefill_args* a, void* stream) {
   p.scale_log2 = a->softmax_scale * kLog2e;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (a->dtype == AKT_FLOAT16) {
-    if (a->head_dim == 64) return launch_prefill<__half, 64>(mq, mk, mv, p, st);
-    return launch_prefill<__half, 128>(mq, mk, mv, p, st);
+    if (a->head_dim == 64)
+      return bn == 64 ? launch_prefill<__half, 64, 64>(mq, mk, mv, p, st) : launch_prefill<__half, 64, 128>(mq, mk, mv, p, st);
+    return bn == 64 ? launch_prefill<__half, 128, 64>(mq, mk, mv, p, st) : launch_prefill<__half, 128, 128>(mq, mk, mv, p, st);
   }
-  if (a->head_dim == 64) return launch_prefill<__nv_bfloat16, 64>(mq, mk, mv, p, st);
-  return launch_prefill<__nv_bfloat16, 128>(mq, mk, mv, p, st);
+  if (a->head_dim == 64)
+    return bn == 64 ? launch_prefill<__nv_bfloat16, 64, 64>(mq, mk, mv, p, st)
+                    : launch_prefill<__nv_bfloat16, 64, 128>(mq, mk, mv, p, st);
+  return bn == 64 ? launch_prefill<__nv_bfloat16, 128, 64>(mq, mk, mv, p, st)
+                  : launch_prefill<__nv_bfloat16, 128, 128>(mq, mk, mv, p, st);
 }

@@ -168,8 +168,9 @@ def time_kernels(fn, iters, dev, flush=None):
     return prof.total_ms / max(prof.launches, 1)
 
 
-def secondary_measurements(dev, iters=20):
-    """The other BASELINE configurations, one kernel each (single GPU)."""
+def secondary_measurements(dev, iters=20, only=None):
+    """The other BASELINE configurations, one kernel each (single GPU).
+    ``only`` restricts the run to one configuration (profiler captures)."""
     from attention_kernel_triton_b200.decode_flash_attention_redundant import flash_attention_decode
     from attention_kernel_triton_b200.magicpig_sparsetoken_decode_flash_attention_redundant_var_len_paged_with_norm import (
         magicpig_sparsetoken_flash_attention_decode_paged)
@@ -183,40 +184,65 @@ def secondary_measurements(dev, iters=20):
     hbm, _ = measured_peaks()
     tf, _ = measured_tflops()
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)  # 256 MB > 126 MB L2
-    out = {}
 
-    c = W.make_prefill(seed=0, device=dev)
-    ms = time_kernels(lambda: flash_attention_prefill(c.Q, c.K, c.V, True, c.softmax_scale, c.group), iters, dev,
-                      flush)
-    out["prefill_cfg0_causal"] = {"tflops": c.flops / ms / 1e9, "ms": ms, "frac_of_bf16_peak": c.flops / ms / 1e9 / tf,
-                                  "gflop": c.flops / 1e9, "l2": "flushed"}
-    c = W.make_prefill(seed=1, device=dev, varlen=True)
-    ms = time_kernels(lambda: flash_attention_prefill_varlen(c.Q, c.K, c.V, True, c.softmax_scale, c.group,
-                                                             c.varlen), iters, dev, flush)
-    out["prefill_cfg1_varlen"] = {"tflops": c.flops / ms / 1e9, "ms": ms, "frac_of_bf16_peak": c.flops / ms / 1e9 / tf,
-                                  "gflop_valid": c.flops / 1e9, "lens": c.varlen.tolist(), "l2": "flushed"}
-    del c
-    for name, kw, fl in [("decode_cfg2", dict(B=8, Hq=64, Hkv=16, L=1024, D=64), True),
-                         ("decode_L4K", dict(B=1, Hq=32, Hkv=8, L=4096, D=128), True),
-                         ("decode_L32K", dict(B=1, Hq=32, Hkv=8, L=32768, D=128), True),
-                         ("decode_L128K", dict(B=1, Hq=32, Hkv=8, L=131072, D=128), False)]:
-        d = W.make_decode(seed=2, device=dev, **kw)
-        ms = time_kernels(lambda: flash_attention_decode(d.q, d.K, d.V, d.softmax_scale, d.group), iters, dev,
-                          flush if fl else None)
-        out[name] = {"gbs": d.bytes / ms / 1e6, "ms": ms, "frac_of_hbm": d.bytes / ms / 1e6 / hbm,
-                     "mb": d.bytes / 1e6, "l2": "flushed" if fl else "inputs larger than L2"}
-    sd = W.make_sparse_dense(seed=41, device=dev)
-    ms = time_kernels(lambda: sparsetoken_flash_attention_decode(sd.q, sd.K, sd.V, sd.sparse_ind, sd.sparse_nnz,
-                                                                 sd.softmax_scale, sd.group), iters, dev, flush)
-    out["sparse_cfg4_dense"] = {"gbs": sd.bytes / ms / 1e6, "ms": ms, "mb": sd.bytes / 1e6, "l2": "flushed"}
-    del sd
-    sp = W.make_sparse_paged(seed=42, device=dev, magicpig=True)
-    ms = time_kernels(lambda: sparsetoken_flash_attention_decode_paged(sp.q, sp.cache, sp.indptr, sp.indices,
-                                                                       sp.sparse_ind, sp.sparse_nnz), iters, dev, flush)
-    out["sparse_cfg4_paged"] = {"gbs": sp.bytes / ms / 1e6, "ms": ms, "mb": sp.bytes / 1e6, "l2": "flushed"}
-    ms = time_kernels(lambda: magicpig_sparsetoken_flash_attention_decode_paged(
-        sp.q, sp.cache, sp.indptr, sp.indices, sp.sparse_ind, sp.sparse_nnz, sp.K, sp.L), iters, dev, flush)
-    out["magicpig_cfg4_paged"] = {"gbs": sp.bytes / ms / 1e6, "ms": ms, "mb": sp.bytes / 1e6, "l2": "flushed"}
+    def prefill_cfg0():
+        c = W.make_prefill(seed=0, device=dev)
+        ms = time_kernels(lambda: flash_attention_prefill(c.Q, c.K, c.V, True, c.softmax_scale, c.group),
+                          iters, dev, flush)
+        return {"tflops": c.flops / ms / 1e9, "ms": ms, "frac_of_bf16_peak": c.flops / ms / 1e9 / tf,
+                "gflop": c.flops / 1e9, "l2": "flushed"}
+
+    def prefill_cfg1():
+        c = W.make_prefill(seed=1, device=dev, varlen=True)
+        ms = time_kernels(lambda: flash_attention_prefill_varlen(c.Q, c.K, c.V, True, c.softmax_scale, c.group,
+                                                                 c.varlen), iters, dev, flush)
+        return {"tflops": c.flops / ms / 1e9, "ms": ms, "frac_of_bf16_peak": c.flops / ms / 1e9 / tf,
+                "gflop_valid": c.flops / 1e9, "lens": c.varlen.tolist(), "l2": "flushed"}
+
+    def decode(kw, fl):
+        def run():
+            d = W.make_decode(seed=2, device=dev, **kw)
+            ms = time_kernels(lambda: flash_attention_decode(d.q, d.K, d.V, d.softmax_scale, d.group), iters, dev,
+                              flush if fl else None)
+            return {"gbs": d.bytes / ms / 1e6, "ms": ms, "frac_of_hbm": d.bytes / ms / 1e6 / hbm,
+                    "mb": d.bytes / 1e6, "l2": "flushed" if fl else "inputs larger than L2"}
+        return run
+
+    def sparse_dense():
+        sd = W.make_sparse_dense(seed=41, device=dev)
+        ms = time_kernels(lambda: sparsetoken_flash_attention_decode(sd.q, sd.K, sd.V, sd.sparse_ind, sd.sparse_nnz,
+                                                                     sd.softmax_scale, sd.group), iters, dev, flush)
+        return {"gbs": sd.bytes / ms / 1e6, "ms": ms, "mb": sd.bytes / 1e6, "l2": "flushed"}
+
+    def sparse_paged(magic):
+        def run():
+            sp = W.make_sparse_paged(seed=42, device=dev, magicpig=True)
+            if magic:
+                fn = lambda: magicpig_sparsetoken_flash_attention_decode_paged(  # noqa: E731
+                    sp.q, sp.cache, sp.indptr, sp.indices, sp.sparse_ind, sp.sparse_nnz, sp.K, sp.L)
+            else:
+                fn = lambda: sparsetoken_flash_attention_decode_paged(  # noqa: E731
+                    sp.q, sp.cache, sp.indptr, sp.indices, sp.sparse_ind, sp.sparse_nnz)
+            ms = time_kernels(fn, iters, dev, flush)
+            return {"gbs": sp.bytes / ms / 1e6, "ms": ms, "mb": sp.bytes / 1e6, "l2": "flushed"}
+        return run
+
+    table = [
+        ("prefill_cfg0_causal", prefill_cfg0),
+        ("prefill_cfg1_varlen", prefill_cfg1),
+        ("decode_cfg2", decode(dict(B=8, Hq=64, Hkv=16, L=1024, D=64), True)),
+        ("decode_L4K", decode(dict(B=1, Hq=32, Hkv=8, L=4096, D=128), True)),
+        ("decode_L32K", decode(dict(B=1, Hq=32, Hkv=8, L=32768, D=128), True)),
+        ("decode_L128K", decode(dict(B=1, Hq=32, Hkv=8, L=131072, D=128), False)),
+        ("sparse_cfg4_dense", sparse_dense),
+        ("sparse_cfg4_paged", sparse_paged(False)),
+        ("magicpig_cfg4_paged", sparse_paged(True)),
+    ]
+    out = {}
+    for name, fn in table:
+        if only is None or only == name:
+            out[name] = fn()
+            torch.cuda.empty_cache()
     return out
 
 
@@ -367,9 +393,15 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-secondary", action="store_true",
                     help="skip the other configurations (prefill, dense decode, sparse)")
+    ap.add_argument("--only", default=None,
+                    help="run just one secondary configuration by name and print it (profiler captures)")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)
+    elif args.only:
+        dev = torch.device("cuda", 0)
+        torch.cuda.set_device(dev)
+        print(json.dumps({args.only: secondary_measurements(dev, iters=args.steps, only=args.only)[args.only]}))
     else:
         run_ours(args)
 
