@@ -132,6 +132,12 @@ SIGNATURES = {
     "akt_sparse_paged": (c_int, [POINTER(SparsePagedArgs), c_void_p, c_size_t, c_void_p]),
     "akt_magicpig_paged_workspace_size": (c_size_t, [POINTER(SparsePagedArgs)]),
     "akt_magicpig_paged": (c_int, [POINTER(SparsePagedArgs), c_void_p, c_size_t, c_void_p]),
+    "akt_sparse_dense_partial": (c_int, [POINTER(SparseDenseArgs), c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]),
+    "akt_sparse_paged_partial": (c_int, [POINTER(SparsePagedArgs), c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]),
+    "akt_magicpig_paged_partial": (c_int, [POINTER(SparsePagedArgs), c_void_p, c_void_p, c_void_p, c_size_t,
+                                           c_void_p]),
+    "akt_lse_merge": (c_int, [c_void_p, c_int64, c_void_p, c_int64, c_int32, c_int64, c_int32, c_void_p, c_int64,
+                              c_int32, c_void_p]),
 }
 
 _lib = None

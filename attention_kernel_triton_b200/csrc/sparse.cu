@@ -65,6 +65,11 @@ struct SparseParams {
   float* part_o;       // [items, G, D]
   float* part_lse;     // [items, G]
   int* unit_offset;    // [B * units + 1]
+  // partial-output mode (KV split across devices): when set, the merge writes
+  // the fp32 normalised O [B, Hq, D] and natural-log LSE [B, Hq] of this
+  // device's tokens instead of the typed output
+  float* out_part_o;
+  float* out_part_lse;
 };
 
 // ---------------------------------------------------------------------------
@@ -357,7 +362,13 @@ __global__ void __launch_bounds__(256) sparse_merge_kernel(const SparseParams p)
       }
     }
     const float val = den > 0.f ? num / den : 0.f;
-    out[(int64_t)b * p.o_sb + (int64_t)(head0 + h) * p.o_sh + (int64_t)d * p.o_sd] = E::from_float(val);
+    if (p.out_part_o) {
+      const int64_t row = (int64_t)b * p.Hq + head0 + h;
+      p.out_part_o[row * D + d] = val;
+      if (d == 0) p.out_part_lse[row] = den > 0.f ? (M + log2f(den)) * kLn2 : -INFINITY;
+    } else {
+      out[(int64_t)b * p.o_sb + (int64_t)(head0 + h) * p.o_sh + (int64_t)d * p.o_sd] = E::from_float(val);
+    }
   }
 }
 
@@ -468,7 +479,8 @@ void fill_common(SparseParams& p, const SparsePlan& pl, void* ws) {
   p.unit_offset = reinterpret_cast<int*>(static_cast<char*>(ws) + pl.off_units);
 }
 
-int paged_entry(const akt_sparse_paged_args* a, void* ws, size_t ws_bytes, void* stream, bool magic) {
+int paged_entry(const akt_sparse_paged_args* a, void* ws, size_t ws_bytes, void* stream, bool magic,
+                float* o_part = nullptr, float* lse_part = nullptr) {
   if (!a) return set_error(AKT_ERR_INVALID, "null args");
   int rc = check_heads(a->batch, a->num_qo_heads, a->num_kv_heads, a->head_dim, a->dtype, a->max_nnz);
   if (rc) return rc;
@@ -498,6 +510,8 @@ int paged_entry(const akt_sparse_paged_args* a, void* ws, size_t ws_bytes, void*
   p.scale_log2 = a->softmax_scale * kLog2e;
   p.inv_sqrt_d = 1.0f / sqrtf((float)a->head_dim);
   fill_common(p, pl, ws);
+  p.out_part_o = o_part;
+  p.out_part_lse = lse_part;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (magic) {
     if (a->dtype == AKT_FLOAT16) return dispatch_sparse<__half, true, true>(p, pl, a->head_dim, st);
@@ -519,7 +533,8 @@ size_t akt_sparse_dense_workspace_size(const akt_sparse_dense_args* a) {
   return make_sparse_plan(a->batch, a->num_qo_heads, a->num_kv_heads, a->head_dim, a->max_nnz).ws_bytes;
 }
 
-int akt_sparse_dense(const akt_sparse_dense_args* a, void* ws, size_t ws_bytes, void* stream) {
+static int sparse_dense_entry(const akt_sparse_dense_args* a, void* ws, size_t ws_bytes, void* stream,
+                              float* o_part, float* lse_part) {
   if (!a) return set_error(AKT_ERR_INVALID, "null args");
   int rc = check_heads(a->batch, a->num_qo_heads, a->num_kv_heads, a->head_dim, a->dtype, a->max_nnz);
   if (rc) return rc;
@@ -547,9 +562,33 @@ int akt_sparse_dense(const akt_sparse_dense_args* a, void* ws, size_t ws_bytes, 
   p.scale_log2 = a->softmax_scale * kLog2e;
   p.inv_sqrt_d = 1.0f / sqrtf((float)a->head_dim);
   fill_common(p, pl, ws);
+  p.out_part_o = o_part;
+  p.out_part_lse = lse_part;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (a->dtype == AKT_FLOAT16) return dispatch_sparse<__half, false, false>(p, pl, a->head_dim, st);
   return dispatch_sparse<__nv_bfloat16, false, false>(p, pl, a->head_dim, st);
+}
+
+int akt_sparse_dense(const akt_sparse_dense_args* a, void* ws, size_t ws_bytes, void* stream) {
+  return sparse_dense_entry(a, ws, ws_bytes, stream, nullptr, nullptr);
+}
+
+int akt_sparse_dense_partial(const akt_sparse_dense_args* a, float* o_part, float* lse_part, void* ws,
+                             size_t ws_bytes, void* stream) {
+  if (!o_part || !lse_part) return set_error(AKT_ERR_INVALID, "partial outputs required");
+  return sparse_dense_entry(a, ws, ws_bytes, stream, o_part, lse_part);
+}
+
+int akt_sparse_paged_partial(const akt_sparse_paged_args* a, float* o_part, float* lse_part, void* ws,
+                             size_t ws_bytes, void* stream) {
+  if (!o_part || !lse_part) return set_error(AKT_ERR_INVALID, "partial outputs required");
+  return paged_entry(a, ws, ws_bytes, stream, false, o_part, lse_part);
+}
+
+int akt_magicpig_paged_partial(const akt_sparse_paged_args* a, float* o_part, float* lse_part, void* ws,
+                               size_t ws_bytes, void* stream) {
+  if (!o_part || !lse_part) return set_error(AKT_ERR_INVALID, "partial outputs required");
+  return paged_entry(a, ws, ws_bytes, stream, true, o_part, lse_part);
 }
 
 size_t akt_sparse_paged_workspace_size(const akt_sparse_paged_args* a) {

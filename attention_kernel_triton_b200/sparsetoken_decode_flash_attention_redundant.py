@@ -19,9 +19,10 @@ from . import _lib
 redundant_len = 16  # reference module constant (SD:7)
 
 
-def sparse_dense_into(out, q, K, V, sparse_ind, sparse_nnz, softmax_scale, GQA_group_size):
-    dev = _lib.require_cuda(q, K, V, out)
-    if not (q.dtype == K.dtype == V.dtype == out.dtype):
+def _sparse_dense_call(entry, out, q, K, V, sparse_ind, sparse_nnz, softmax_scale, GQA_group_size, partial=None):
+    """Shared launcher; ``partial=(o_part, lse_part)`` selects the partial-output entry point."""
+    dev = _lib.require_cuda(q, K, V)
+    if not (q.dtype == K.dtype == V.dtype) or (out is not None and out.dtype != q.dtype):
         raise TypeError("q, K, V and the output must share one dtype")
     B, Hq, _, D = q.shape
     Hkv = K.shape[1]
@@ -31,6 +32,7 @@ def sparse_dense_into(out, q, K, V, sparse_ind, sparse_nnz, softmax_scale, GQA_g
     nnz = _lib.as_int32(sparse_nnz, dev)
     t = {"q": q, "K": K, "V": V}
     L = _lib.lib()
+    fn = getattr(L, entry)
 
     def call():
         a = _lib.SparseDenseArgs()
@@ -44,14 +46,18 @@ def sparse_dense_into(out, q, K, V, sparse_ind, sparse_nnz, softmax_scale, GQA_g
         (a.ind_stride_batch, a.ind_stride_head, a.ind_stride_pos), (a.nnz_stride_batch, a.nnz_stride_head) = \
             _lib.index_strides(ind, nnz)
         a.sparse_ind, a.sparse_nnz = ind.data_ptr(), nnz.data_ptr()
-        a.out = out.data_ptr()
-        a.out_stride_batch, a.out_stride_head, a.out_stride_dim = out.stride(0), out.stride(1), out.stride(3)
+        if out is not None:
+            a.out = out.data_ptr()
+            a.out_stride_batch, a.out_stride_head, a.out_stride_dim = out.stride(0), out.stride(1), out.stride(3)
         a.batch, a.num_qo_heads, a.num_kv_heads, a.seq_len, a.head_dim = B, Hq, Hkv, KK.shape[2], D
         a.max_nnz = ind.shape[2]
         a.dtype = _lib.dtype_code(qq)
         a.softmax_scale = float(softmax_scale)
         ws = _lib.workspace(L.akt_sparse_dense_workspace_size(ctypes.byref(a)), dev)
-        return L.akt_sparse_dense(ctypes.byref(a), ws.data_ptr(), ws.numel(), _lib.stream_ptr(dev))
+        if partial is not None:
+            return fn(ctypes.byref(a), partial[0].data_ptr(), partial[1].data_ptr(), ws.data_ptr(), ws.numel(),
+                      _lib.stream_ptr(dev))
+        return fn(ctypes.byref(a), ws.data_ptr(), ws.numel(), _lib.stream_ptr(dev))
 
     def contiguous():
         for k in t:
@@ -59,7 +65,21 @@ def sparse_dense_into(out, q, K, V, sparse_ind, sparse_nnz, softmax_scale, GQA_g
 
     with torch.cuda.device(dev):
         _lib.run_with_layout_retry(call, contiguous)
+
+
+def sparse_dense_into(out, q, K, V, sparse_ind, sparse_nnz, softmax_scale, GQA_group_size):
+    """Write the sparse-token decode into ``out [B, Hq, 1, D]``."""
+    _lib.require_cuda(out)
+    _sparse_dense_call("akt_sparse_dense", out, q, K, V, sparse_ind, sparse_nnz, softmax_scale, GQA_group_size)
     return out
+
+
+def sparse_dense_partial(o_part, lse_part, q, K, V, sparse_ind, sparse_nnz, softmax_scale, GQA_group_size):
+    """Partial over this device's tokens: fp32 ``o_part [B, Hq, D]`` normalised over the
+    kept tokens present in ``K``/``V``, natural-log ``lse_part [B, Hq]`` (-inf if none)."""
+    _sparse_dense_call("akt_sparse_dense_partial", None, q, K, V, sparse_ind, sparse_nnz, softmax_scale,
+                       GQA_group_size, partial=(o_part, lse_part))
+    return o_part, lse_part
 
 
 def sparsetoken_flash_attention_decode(q, K, V, sparse_ind, sparse_nnz, softmax_scale, GQA_group_size):

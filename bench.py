@@ -227,6 +227,12 @@ def secondary_measurements(dev, iters=20, only=None):
             return {"gbs": sp.bytes / ms / 1e6, "ms": ms, "mb": sp.bytes / 1e6, "l2": "flushed"}
         return run
 
+    def sparse_128k():
+        sd = W.make_sparse_dense(B=1, Hq=32, Hkv=8, L=131072, D=128, keep_p=0.02, seed=12, device=dev, L_max=4096)
+        ms = time_kernels(lambda: sparsetoken_flash_attention_decode(sd.q, sd.K, sd.V, sd.sparse_ind, sd.sparse_nnz,
+                                                                     sd.softmax_scale, sd.group), iters, dev, flush)
+        return {"gbs": sd.bytes / ms / 1e6, "ms": ms, "mb": sd.bytes / 1e6, "l2": "flushed"}
+
     table = [
         ("prefill_cfg0_causal", prefill_cfg0),
         ("prefill_cfg1_varlen", prefill_cfg1),
@@ -237,6 +243,7 @@ def secondary_measurements(dev, iters=20, only=None):
         ("sparse_cfg4_dense", sparse_dense),
         ("sparse_cfg4_paged", sparse_paged(False)),
         ("magicpig_cfg4_paged", sparse_paged(True)),
+        ("sparse_128k_single_sequence", sparse_128k),
     ]
     out = {}
     for name, fn in table:
@@ -244,6 +251,39 @@ def secondary_measurements(dev, iters=20, only=None):
             out[name] = fn()
             torch.cuda.empty_cache()
     return out
+
+
+def kv_split_measurement(dev, pg, world, rank, steps=50):
+    """128K-token single-sequence sparse decode split along the key axis over
+    all ranks: partial on each GPU, NCCL all-gather of [O | LSE], LSE merge.
+    Every rank takes the same collective steps; time is the max over ranks."""
+    from attention_kernel_triton_b200.distributed import shard_range, shard_sparse_lists, sparsetoken_decode_kv_split
+    c = W.make_sparse_dense(B=1, Hq=32, Hkv=8, L=131072, D=128, keep_p=0.02, seed=12, device=dev, L_max=4096)
+    lo, hi = shard_range(131072, world, rank)
+    ind, nnz = shard_sparse_lists(c.sparse_ind, c.sparse_nnz, lo, hi)
+    K, V = c.K[:, :, lo:hi].contiguous(), c.V[:, :, lo:hi].contiguous()
+    total_bytes = c.bytes
+    del c
+
+    def step():
+        return sparsetoken_decode_kv_split(q, K, V, ind, nnz, scale, 4)
+    q = W.make_sparse_dense(B=1, Hq=32, Hkv=8, L=16, D=128, seed=12, device=dev).q
+    scale = 1.0 / math.sqrt(128)
+    for _ in range(3):
+        step()
+    pg.barrier()
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize(dev)
+    t = torch.tensor([e0.elapsed_time(e1) / steps], dtype=torch.float64, device=dev)
+    pg.all_reduce(t, op=pg.ReduceOp.MAX)
+    ms = float(t[0])
+    return {"gbs": total_bytes / ms / 1e6, "ms": ms, "n_gpus": world, "mb": total_bytes / 1e6,
+            "allgather_bytes_per_rank": 32 * (128 + 1) * 4, "steps": steps}
 
 
 def run_ours(args):
@@ -344,6 +384,10 @@ def run_ours(args):
         del c
         torch.cuda.empty_cache()
         secondary = secondary_measurements(dev)
+    elif world > 1 and not args.no_secondary:
+        del c
+        torch.cuda.empty_cache()
+        secondary = {"kv_split_128k": kv_split_measurement(dev, pg, world, rank)}
     if rank == 0:
         cpu = None
         if world == 1 and not args.no_cpu_baseline:

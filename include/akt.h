@@ -234,6 +234,30 @@ int akt_sparse_paged(const akt_sparse_paged_args* args, void* workspace, size_t 
 size_t akt_magicpig_paged_workspace_size(const akt_sparse_paged_args* args);
 int akt_magicpig_paged(const akt_sparse_paged_args* args, void* workspace, size_t workspace_bytes, void* stream);
 
+/* ------------------------------------------------------------------------ */
+/* KV split across devices (long single-sequence sparse decode)             */
+/* No reference counterpart (the reference keeps no LSE; its store is       */
+/* commented out at prefill_flash_attention.py:331-334).  The *_partial     */
+/* entry points run the matching sparse decode over this device's tokens    */
+/* and, instead of the typed output, write the fp32 output normalised over  */
+/* those tokens, o_part [batch, num_qo_heads, head_dim], and its natural-   */
+/* log sum-exp, lse_part [batch, num_qo_heads] (-inf where no token was     */
+/* kept).  akt_lse_merge combines num_parts such partials into out rows of  */
+/* head_dim elements (row stride out_row_stride); part i's O starts at      */
+/* o_parts + i * o_part_stride and its LSE at lse_parts + i *               */
+/* lse_part_stride (floats), so one all-gathered [O | LSE] buffer per       */
+/* device merges in place.                                                  */
+/* ------------------------------------------------------------------------ */
+int akt_sparse_dense_partial(const akt_sparse_dense_args* args, float* o_part, float* lse_part, void* workspace,
+                             size_t workspace_bytes, void* stream);
+int akt_sparse_paged_partial(const akt_sparse_paged_args* args, float* o_part, float* lse_part, void* workspace,
+                             size_t workspace_bytes, void* stream);
+int akt_magicpig_paged_partial(const akt_sparse_paged_args* args, float* o_part, float* lse_part,
+                               void* workspace, size_t workspace_bytes, void* stream);
+int akt_lse_merge(const float* o_parts, int64_t o_part_stride, const float* lse_parts, int64_t lse_part_stride,
+                  int32_t num_parts, int64_t rows, int32_t head_dim, void* out, int64_t out_row_stride,
+                  int32_t dtype, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,32 @@
+"""CPU stand-ins for the two compute steps of the KV-split sparse decode, used
+only to exercise the host logic (sharding, all-gather, ordering) under gloo."""
+import math
+
+import torch
+
+from oracle import naive as N
+
+
+def oracle_partial(buf, rows, D, q, K, V, ind, nnz, scale, group):
+    B, Hq = q.shape[0], q.shape[1]
+    o = buf[: rows * D].view(B, Hq, D)
+    lse = buf[rows * D:].view(B, Hq)
+    qf, Kf, Vf = q.float(), K.float(), V.float()
+    for b in range(B):
+        for h in range(Hq):
+            n = int(nnz[b, h])
+            if n <= 0:
+                o[b, h] = 0
+                lse[b, h] = -math.inf
+                continue
+            idx = ind[b, h, :n].long()
+            s = (Kf[b, h // group, idx] @ qf[b, h, 0]) * scale
+            lse[b, h] = torch.logsumexp(s, 0)
+            o[b, h] = torch.softmax(s, 0) @ Vf[b, h // group, idx]
+
+
+def oracle_merge(out, recv, rows, D):
+    n = recv.shape[0]
+    o = recv[:, : rows * D].view(n, rows, D)
+    lse = recv[:, rows * D:]
+    out.view(rows, D).copy_(N.lse_merge_reference(o, lse).to(out.dtype))

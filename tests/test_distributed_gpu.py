@@ -1,0 +1,129 @@
+"""GPU checks of the KV-split sparse decode: per-rank CUDA partials merged by
+akt_lse_merge (ranks emulated one after another on one GPU), the merge kernel
+against the oracle, and the real NCCL path on 2 GPUs when the box has them.
+
+Tolerance: max-abs <= 2e-3 against the fp32 oracle, no NaNs.
+"""
+import math
+import os
+import socket
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+from oracle import naive as N
+
+from attention_kernel_triton_b200 import _lib
+from attention_kernel_triton_b200 import workloads as W
+from attention_kernel_triton_b200.distributed import (lse_merge_into, shard_range, shard_sparse_lists,
+                                                      sparsetoken_decode_kv_split)
+from attention_kernel_triton_b200.sparsetoken_decode_flash_attention_redundant import (
+    sparse_dense_partial, sparsetoken_flash_attention_decode)
+
+pytestmark = pytest.mark.gpu
+TOL = 2e-3
+DEV = "cuda"
+
+
+@pytest.fixture(autouse=True)
+def device_status_clean():
+    _lib.device_status(0, clear=True)
+    yield
+    assert _lib.device_status(0) == 0, "a kernel recorded an error"
+
+
+def emulate_split(c, world):
+    B, Hq, _, D = c.q.shape
+    L = c.K.shape[2]
+    rows = B * Hq
+    recv = torch.empty((world, rows * D + rows), dtype=torch.float32, device=DEV)
+    for r in range(world):
+        lo, hi = shard_range(L, world, r)
+        ind, nnz = shard_sparse_lists(c.sparse_ind, c.sparse_nnz, lo, hi)
+        sparse_dense_partial(recv[r, : rows * D].view(rows, D), recv[r, rows * D:], c.q, c.K[:, :, lo:hi],
+                             c.V[:, :, lo:hi], ind, nnz, c.softmax_scale, c.group)
+    out = torch.empty((B, Hq, 1, D), dtype=c.q.dtype, device=DEV)
+    lse_merge_into(out, recv, rows, D)
+    return out
+
+
+@pytest.mark.parametrize("world", [1, 2, 4, 8])
+def test_kv_split_emulated_matches_oracle(world):
+    c = W.make_sparse_dense(B=2, Hq=8, Hkv=2, L=4000, D=128, keep_p=0.03, seed=10 + world, device=DEV)
+    out = emulate_split(c, world)
+    ref = N.sparsetoken_naive_decode(c.q, c.K, c.V, c.sparse_ind, c.sparse_nnz, c.softmax_scale, c.group)
+    assert not torch.isnan(out).any()
+    assert (out.float().cpu() - ref).abs().max().item() <= TOL
+    single = sparsetoken_flash_attention_decode(c.q, c.K, c.V, c.sparse_ind, c.sparse_nnz, c.softmax_scale, c.group)
+    assert (out.float() - single.float()).abs().max().item() <= TOL
+
+
+def test_kv_split_128k_single_sequence_over_8_shards():
+    # BASELINE cfg4: 128K-token single sequence, keep 2% per kv head, split over 8 ranks
+    c = W.make_sparse_dense(B=1, Hq=32, Hkv=8, L=131072, D=128, keep_p=0.02, seed=12, device=DEV, L_max=4096)
+    out = emulate_split(c, 8)
+    ref = N.sparsetoken_naive_decode(c.q, c.K, c.V, c.sparse_ind, c.sparse_nnz, c.softmax_scale, c.group)
+    assert (out.float().cpu() - ref).abs().max().item() <= TOL
+
+
+def test_lse_merge_matches_oracle_with_empty_parts():
+    g = torch.Generator().manual_seed(3)
+    n, rows, D = 5, 37, 64
+    o = torch.randn(n, rows, D, generator=g)
+    lse = torch.randn(n, rows, generator=g) * 4
+    lse[1] = -math.inf          # a part with no keys
+    lse[:, 5] = -math.inf       # a row with no keys anywhere
+    recv = torch.cat([o.reshape(n, -1), lse], dim=1).to(DEV)
+    out = torch.empty(rows, D, dtype=torch.float16, device=DEV)
+    lse_merge_into(out, recv, rows, D)
+    ref = N.lse_merge_reference(o, lse)
+    assert (out.float().cpu() - ref.float()).abs().max().item() <= TOL
+    assert torch.all(out[5] == 0)
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _nccl_worker(rank, world, port, q):
+    import datetime
+
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                            timeout=datetime.timedelta(seconds=60))
+    try:
+        c = W.make_sparse_dense(B=1, Hq=32, Hkv=8, L=32768, D=128, keep_p=0.02, seed=21)  # CPU, same on all ranks
+        lo, hi = shard_range(32768, world, rank)
+        ind, nnz = shard_sparse_lists(c.sparse_ind, c.sparse_nnz, lo, hi)
+        out = sparsetoken_decode_kv_split(c.q.to(dev), c.K[:, :, lo:hi].to(dev), c.V[:, :, lo:hi].to(dev),
+                                          ind.to(dev), nnz.to(dev), c.softmax_scale, c.group)
+        torch.cuda.synchronize(dev)
+        ref = N.sparsetoken_naive_decode(c.q, c.K, c.V, c.sparse_ind, c.sparse_nnz, c.softmax_scale, c.group)
+        q.put((rank, float((out.float().cpu() - ref).abs().max())))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_kv_split_nccl_two_gpus():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_nccl_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=600)
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    errs = dict(q.get(timeout=5) for _ in range(2))
+    assert max(errs.values()) <= TOL, errs
