@@ -35,6 +35,7 @@ sys.path.insert(0, ROOT)
 from attention_kernel_triton_b200 import workloads as W  # noqa: E402
 
 METRIC = "paged decode HBM GB/s"
+CFG3_TRAFFIC_BYTES = 4.51e9 + 7.19e6  # ncu: read 4.51 GB + write 7.19 MB per split-KV launch
 WORKLOAD = ("cfg3 paged var-len GQA decode: B=64 Hq=32 Hkv=8 D=128 fp16 page_size=16 "
             "lens U[512,32768] seeded, random physical page order")
 
@@ -410,7 +411,11 @@ def run_ours(args):
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_source": peak_kind,
                          "kernel": "decode_splitkv_kernel<half,128,4,paged>",
-                         "kernel_ms": kern_ms, "traffic": None},
+                         "kernel_ms": kern_ms,
+                         # dram__bytes_read.sum + dram__bytes_write.sum of one launch of this
+                         # kernel on this workload, from an ncu capture of the same command
+                         "traffic": CFG3_TRAFFIC_BYTES if args.batch == 64 else None,
+                         "traffic_over_algorithmic": CFG3_TRAFFIC_BYTES / nbytes if args.batch == 64 else None},
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_val, "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "ms_per_step": e2e_ms},
