@@ -6,26 +6,39 @@
 // O = softmax(Q K^T * s [+ top-left causal mask]) V with GQA kv head h / G,
 // fp32 accumulation, P rounded to the input dtype before P.V (PF:94); the
 // var-len variant skips query rows past each sequence's length (PV:186-187)
-// and masks no keys (the reference does not either).
+// and masks no keys beyond the causal mask (the reference does not either).
 //
-// One CTA = one 128-row query tile of one (batch, head).  Warp roles:
-//   warps 0-3  softmax warpgroup: thread t owns query row t = TMEM lane t;
-//              reads S with tcgen05.ld, writes P (input dtype) to shared
-//              memory in the 128B-swizzled K-major layout, rescales O in
-//              TMEM when its running max moves, and runs the epilogue.
-//   warp 4     TMA producer: Q once, then K_j and V_j into a ring of stages.
-//   warp 5     TMEM allocator and single-thread MMA issuer:
-//              S_j = Q K_j^T  (M=128, N=128, K=D)   into TMEM S[j%2]
-//              O  += P_j V_j  (M=128, N=D,  K=128)  into TMEM O
+// Persistent CTAs (one per SM) walk a list of work items, heaviest causal
+// tiles first.  An item is two 128-row query tiles ("slots") that read the
+// same K/V: two qo heads of one kv head at the same rows when the GQA group
+// is even, else two consecutive query tiles of one head.  Warp roles:
+//   warps 0-3 / 4-7  softmax warpgroup of slot 0 / 1: thread i owns query row
+//              i = TMEM lane i; reads S with tcgen05.ld, writes P (input
+//              dtype) back to TMEM with tcgen05.st, rescales O in TMEM when
+//              its running max moves, and writes the normalised output.
+//   warp 8     TMA producer: lane 0 loads Q and the K ring, lane 1 the V ring.
+//   warp 9     TMEM allocator and MMA issuer (one elected lane):
+//              S_t = Q_t K_j^T (M=128, N=BN, K=D; A and B in shared memory)
+//              O_t += P_t V_j   (M=128, N=D,  K=BN; A = P in TMEM, B = V)
+// TMEM (512 columns): S[2] (BN each), O[2] (D each), P[2] (BN/2 each, two
+// 16-bit values per column).  With S and P apart, S for key tile j+1 is
+// computed while the softmax still works on tile j; the only per-tile wait
+// of a softmax warpgroup is for its previous P.V before it overwrites P.
+//
 // The running max used for exponentiation only moves when the row max grows
 // by more than 8 (log2 units), so O is rescaled rarely (P <= 2^8 stays exact
-// enough in fp16/bf16 relative terms; the final O/l is unchanged).
+// enough in fp16/bf16 relative terms; the final O/l is unchanged).  On key
+// tiles without masking a share of the exponentials is evaluated on the FMA
+// pipe by a polynomial (exp2_poly2) instead of the MUFU unit, whose 16
+// results per clock per SM would otherwise bound a head_dim-64 kernel.
 #include "common.cuh"
 #include "profile.cuh"
 
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <algorithm>
+#include <climits>
 #include <cstdlib>
 #include <mutex>
 #include <string>
@@ -36,47 +49,42 @@ int set_error(int code, const std::string& msg);
 
 namespace {
 
-constexpr int BM = 128;            // query rows per CTA
-constexpr int kThreads = 192;
+constexpr int BM = 128;            // query rows per slot
+constexpr int kSlots = 2;          // query tiles per work item
+constexpr int kThreads = 320;      // 2 softmax warpgroups + producer warp + MMA warp
+constexpr int kLoadWarp = 8;
+constexpr int kMmaWarp = 9;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 
-__host__ __device__ constexpr int pow2_at_least(int x) {
-  int v = 32;
-  while (v < x) v *= 2;
-  return v;
-}
+// 8-element chunks of a row evaluated by the FMA-pipe polynomial (of BN/8) on
+// key tiles without masking; the rest use MUFU ex2.
+#ifndef AKT_PREFILL_POLY_CHUNKS
+#define AKT_PREFILL_POLY_CHUNKS 0
+#endif
 
-// Tile configuration per (head_dim D, keys per tile BN).  TMEM holds S
-// (NSB buffers of BN fp32 columns) and O (D columns); shared memory holds Q,
-// a two-stage K/V ring and one P tile.  Smaller footprints let more CTAs (and
-// so more softmax warpgroups) share an SM:
-//   D=64,  BN=64 : TMEM 128 cols,  64 KB smem -> 3 CTAs/SM
-//   D=64,  BN=128: TMEM 256 cols, 112 KB smem -> 2 CTAs/SM
-//   D=128, BN=64 : TMEM 256 cols, 112 KB smem -> 2 CTAs/SM
-//   D=128, BN=128: TMEM 512 cols (S double-buffered), 192 KB -> 1 CTA/SM
-template <int D, int BN_>
+// Tile configuration per head_dim D.  Keys per tile BN is chosen so that
+// S[2], O[2] and P[2] fit the 512 TMEM columns of one SM:
+//   D=64 : BN=128 -> 256 + 128 + 128 = 512 columns, smem 32 KB Q + rings
+//   D=128: BN=64  -> 128 + 256 +  64 = 448 columns, smem 64 KB Q + rings
+template <int D>
 struct Cfg {
-  static constexpr int BN = BN_;
+  static constexpr int BN = D == 64 ? 128 : 64;
   static constexpr int DB = D / 64;                       // 64-element (128 B) swizzle blocks per row
-  static constexpr int NSB = (D == 128 && BN == 128) ? 2 : 1;
-  static constexpr int COL_O = NSB * BN;
-  static constexpr int TMEM_COLS = pow2_at_least(COL_O + D);
-  // K and V rings are separate: a K stage is released when its S MMA is done,
-  // a V stage when its P.V MMA is done, so K loads run further ahead.
-  static constexpr int NSK = (D == 64 && BN == 64) ? 3 : 2;
-  static constexpr int NSV = 2;
-  static constexpr int NP = 1;                            // P buffers
-  static constexpr uint32_t Q_BYTES = BM * D * 2;
+  static constexpr int COL_S = 0;                         // + slot * BN
+  static constexpr int COL_O = 2 * BN;                    // + slot * D
+  static constexpr int COL_P = 2 * BN + 2 * D;            // + slot * BN / 2
+  static constexpr int TMEM_COLS = 512;
+  static_assert(COL_P + BN <= TMEM_COLS, "TMEM budget");
+  static constexpr int NSK = 3, NSV = 3;                  // K / V ring stages
+  static constexpr int CHUNKS = BN / 8;
+  static constexpr int POLY = AKT_PREFILL_POLY_CHUNKS < CHUNKS ? AKT_PREFILL_POLY_CHUNKS : CHUNKS;
+  static constexpr uint32_t Q_BYTES = BM * D * 2;         // one slot
   static constexpr uint32_t KV_BYTES = BN * D * 2;        // one K or V tile
-  static constexpr uint32_t P_BYTES = BM * BN * 2;
   static constexpr uint32_t OFF_Q = 0;
-  static constexpr uint32_t OFF_K = OFF_Q + Q_BYTES;
+  static constexpr uint32_t OFF_K = OFF_Q + kSlots * Q_BYTES;
   static constexpr uint32_t OFF_V = OFF_K + NSK * KV_BYTES;
-  static constexpr uint32_t OFF_P = OFF_V + NSV * KV_BYTES;
-  static constexpr uint32_t OFF_BAR = OFF_P + NP * P_BYTES;
+  static constexpr uint32_t OFF_BAR = OFF_V + NSV * KV_BYTES;
   static constexpr uint32_t SMEM = OFF_BAR + 256;         // + barriers (base is 1024-aligned)
-  static constexpr int CTAS_PER_SM = (SMEM + 1024) * 3 <= 228 * 1024 && TMEM_COLS * 3 <= 512 ? 3
-                                     : (SMEM + 1024) * 2 <= 228 * 1024 && TMEM_COLS * 2 <= 512 ? 2 : 1;
 };
 
 struct PrefillParams {
@@ -85,9 +93,50 @@ struct PrefillParams {
   const int32_t* varlen;     // [B] or null
   int B, Hq, Hkv, S, group;
   int n_q_tiles;
+  int n_items;
+  int pair_heads;            // 1: slots are qo heads 2p, 2p+1 at the same rows; 0: query tiles 2p, 2p+1 of one head
   int causal;
   float scale_log2;
 };
+
+// One work item: the key-tile count of each slot (0 = slot has no valid rows).
+struct Item {
+  int b, kvh, seq_len, L;
+  int h[kSlots], q0[kSlots], nkv[kSlots];
+};
+
+// Item i of the list; every role of the CTA decodes the same item.  Items are
+// ordered by query-tile index, last (longest causal row range) first.
+__device__ __forceinline__ Item decode_item(const PrefillParams& p, int i, int BN) {
+  Item it;
+  if (p.pair_heads) {
+    const int hp_n = p.Hq / 2, per = p.B * hp_n;
+    const int qt = p.n_q_tiles - 1 - i / per, r = i % per;
+    it.b = r / hp_n;
+    const int hp = r % hp_n;
+    it.h[0] = 2 * hp;
+    it.h[1] = 2 * hp + 1;
+    it.q0[0] = it.q0[1] = qt * BM;
+  } else {
+    const int per = p.B * p.Hq, n_qp = (p.n_q_tiles + 1) / 2;
+    const int qp = n_qp - 1 - i / per, r = i % per;
+    it.b = r / p.Hq;
+    it.h[0] = it.h[1] = r % p.Hq;
+    it.q0[0] = 2 * qp * BM;
+    it.q0[1] = (2 * qp + 1) * BM;
+  }
+  it.kvh = it.h[0] / p.group;
+  it.seq_len = p.varlen ? min(max(__ldg(p.varlen + it.b), 0), p.S) : p.S;
+  it.L = 0;
+#pragma unroll
+  for (int t = 0; t < kSlots; ++t) {
+    // causal: rows past seq_len are zeroed, so keys past it are never needed
+    const int last_key = p.causal ? min(it.q0[t] + BM, it.seq_len) - 1 : p.S - 1;
+    it.nkv[t] = it.q0[t] < it.seq_len ? last_key / BN + 1 : 0;
+    it.L = max(it.L, it.nkv[t]);
+  }
+  return it;
+}
 
 // -------------------------------------------------------------------------
 // PTX helpers
@@ -113,6 +162,18 @@ __device__ __forceinline__ void mma_f16(uint32_t tmem_d, uint64_t a, uint64_t b,
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
       "l"(a), "l"(b), "r"(idesc), "r"(acc)
+      : "memory");
+}
+
+// A operand from TMEM (K-major, two 16-bit values per 32-bit column, row i
+// in lane i), B from shared memory through its descriptor
+__device__ __forceinline__ void mma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t b, uint32_t idesc,
+                                           uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(b), "r"(idesc), "r"(acc)
       : "memory");
 }
 
@@ -171,6 +232,35 @@ __device__ __forceinline__ bool elect_one() {
   return pred != 0;
 }
 
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+// 2^x on the FMA/ALU pipes for a pair of values, x <= ~8 (larger arguments are
+// not produced: the running max trails the row max by at most 8).  x is
+// clamped to -126 (2^-126 rounds to zero in fp16/bf16), split as x = j + f with
+// j = round-to-nearest(x) read from the low mantissa bits of x + 1.5*2^23 and
+// f in [-0.5, 0.5]; 2^f = 1 + f(c1 + f(c2 + f c3)), a degree-3 fit with the
+// constant term fixed at 1 and the other coefficients minimising the maximum
+// relative error on [-0.5, 0.5] (1.0e-4, below half an fp16 ulp); 2^j is added
+// to the exponent field.
+__device__ __forceinline__ float2 exp2_poly2(float2 x) {
+  constexpr float kShift = 12582912.0f;  // 1.5 * 2^23
+  constexpr float c1 = 0.693282961845398f, c2 = 0.2422109991312027f, c3 = 0.055008918046951294f;
+  x.x = fmaxf(x.x, -126.f);
+  x.y = fmaxf(x.y, -126.f);
+  const float2 t = __fadd2_rn(x, make_float2(kShift, kShift));
+  const float2 j = __fadd2_rn(t, make_float2(-kShift, -kShift));
+  const float2 f = __ffma2_rn(j, make_float2(-1.f, -1.f), x);
+  float2 q = __ffma2_rn(make_float2(c3, c3), f, make_float2(c2, c2));
+  q = __ffma2_rn(q, f, make_float2(c1, c1));
+  q = __ffma2_rn(q, f, make_float2(1.f, 1.f));
+  return make_float2(__uint_as_float(__float_as_uint(q.x) + (__float_as_uint(t.x) << 23)),
+                     __uint_as_float(__float_as_uint(q.y) + (__float_as_uint(t.y) << 23)));
+}
+
 template <typename T>
 __device__ __forceinline__ uint32_t pack_p(float a, float b) {
   return Elem<T>::pack2(a, b);
@@ -179,11 +269,12 @@ __device__ __forceinline__ uint32_t pack_p(float a, float b) {
 // -------------------------------------------------------------------------
 // kernel
 // -------------------------------------------------------------------------
-template <typename T, int D, int BN>
-__global__ void __launch_bounds__(kThreads, (Cfg<D, BN>::CTAS_PER_SM))
+template <typename T, int D>
+__global__ void __launch_bounds__(kThreads, 1)
     prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                        const __grid_constant__ CUtensorMap tmV, const PrefillParams p) {
-  using C = Cfg<D, BN>;
+  using C = Cfg<D>;
+  constexpr int BN = C::BN;
   constexpr int fmt = std::is_same<T, __half>::value ? 0 : 1;
   constexpr uint32_t IDESC_S = idesc_f16(fmt, BM, BN, 0);
   constexpr uint32_t IDESC_PV = idesc_f16(fmt, BM, D, 1);
@@ -194,41 +285,31 @@ __global__ void __launch_bounds__(kThreads, (Cfg<D, BN>::CTAS_PER_SM))
     return;
   }
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
-  uint64_t* q_full = bars + 0;
-  uint64_t* k_full = bars + 1;                   // [NSK]
+  uint64_t* q_full = bars;                       // [2]
+  uint64_t* q_empty = q_full + kSlots;           // [2]
+  uint64_t* k_full = q_empty + kSlots;           // [NSK]
   uint64_t* k_empty = k_full + C::NSK;           // [NSK]
   uint64_t* v_full = k_empty + C::NSK;           // [NSV]
   uint64_t* v_empty = v_full + C::NSV;           // [NSV]
-  uint64_t* s_full = v_empty + C::NSV;           // [NSB]
-  uint64_t* s_empty = s_full + C::NSB;           // [NSB]
-  uint64_t* p_full = s_empty + C::NSB;           // [NP]
-  uint64_t* p_empty = p_full + C::NP;            // [NP]
-  uint64_t* o_done = p_empty + C::NP;            // 1
-  uint64_t* mma_idle = o_done + 1;               // 1
+  uint64_t* s_full = v_empty + C::NSV;           // [2]
+  uint64_t* s_empty = s_full + kSlots;           // [2]
+  uint64_t* p_full = s_empty + kSlots;           // [2]
+  uint64_t* pv_done = p_full + kSlots;           // [2]
+  uint64_t* mma_idle = pv_done + kSlots;         // 1
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_idle + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int q_tile = p.n_q_tiles - 1 - (int)blockIdx.x;  // heaviest causal tiles first
-  const int h = blockIdx.y, b = blockIdx.z;
-  const int q0 = q_tile * BM;
-  const int seq_len = p.varlen ? min(max(p.varlen[b], 0), p.S) : p.S;
-
-  // ---- tile entirely past the sequence (var-len padding): zeros, no MMA
-  if (q0 >= seq_len) {
-    T* o = static_cast<T*>(p.o) + (int64_t)b * p.o_sb + (int64_t)h * p.o_sh;
-    for (int e = threadIdx.x; e < BM * (D / 8); e += kThreads) {
-      const int r = q0 + e / (D / 8), c = (e % (D / 8)) * 8;
-      if (r < p.S) *reinterpret_cast<uint4*>(o + (int64_t)r * p.o_ss + c) = make_uint4(0, 0, 0, 0);
-    }
-    return;
-  }
-  const int last_key = p.causal ? min(q0 + BM, seq_len) - 1 : p.S - 1;  // causal: rows past seq_len are zeroed
-  const int n_kv = last_key / BN + 1;
-  const int kvh = h / p.group;
 
   if (threadIdx.x == 0) {
-    mbar_init(q_full, 1);
+    for (int t = 0; t < kSlots; ++t) {
+      mbar_init(&q_full[t], 1);
+      mbar_init(&q_empty[t], 1);
+      mbar_init(&s_full[t], 1);
+      mbar_init(&s_empty[t], 4);
+      mbar_init(&p_full[t], 4);
+      mbar_init(&pv_done[t], 1);
+    }
     for (int s = 0; s < C::NSK; ++s) {
       mbar_init(&k_full[s], 1);
       mbar_init(&k_empty[s], 1);
@@ -237,20 +318,11 @@ __global__ void __launch_bounds__(kThreads, (Cfg<D, BN>::CTAS_PER_SM))
       mbar_init(&v_full[s], 1);
       mbar_init(&v_empty[s], 1);
     }
-    for (int s = 0; s < C::NSB; ++s) {
-      mbar_init(&s_full[s], 1);
-      mbar_init(&s_empty[s], 4);
-    }
-    for (int s = 0; s < C::NP; ++s) {
-      mbar_init(&p_full[s], 4);
-      mbar_init(&p_empty[s], 1);
-    }
-    mbar_init(o_done, 1);
     mbar_init(mma_idle, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 5) {
+  if (warp == kMmaWarp) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
                  "r"(C::TMEM_COLS));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
@@ -271,91 +343,129 @@ __global__ void __launch_bounds__(kThreads, (Cfg<D, BN>::CTAS_PER_SM))
     return __all_sync(0xffffffffu, wait(bar, parity)) != 0;
   };
 
-  if (warp == 4) {
+  if (warp == kLoadWarp) {
     // ========================= TMA producers =========================
-    // lane 0: Q, then the K ring; lane 1: the V ring (independent waits)
+    // Phases continue across items: counters are global to the CTA.
     if (lane == 0) {
-      unsigned char* sQ = smem + C::OFF_Q;
-      mbar_arrive_expect_tx(q_full, C::Q_BYTES);
+      uint32_t qc[kSlots] = {0, 0}, gk = 0;
+      bool ok = true;
+      for (int i = blockIdx.x; ok && i < p.n_items; i += gridDim.x) {
+        const Item it = decode_item(p, i, BN);
 #pragma unroll
-      for (int db = 0; db < C::DB; ++db) tma_load_4d(sQ + db * BM * 128, &tmQ, db * 64, q0, h, b, q_full);
-      int issued = 0;
-      for (int j = 0; j < n_kv; ++j) {
-        const int st = j % C::NSK;
-        if (j >= C::NSK && !wait(&k_empty[st], ((j / C::NSK) - 1) & 1)) break;
-        unsigned char* sK = smem + C::OFF_K + st * C::KV_BYTES;
-        mbar_arrive_expect_tx(&k_full[st], C::KV_BYTES);
+        for (int t = 0; t < kSlots; ++t) {
+          if (!it.nkv[t]) continue;
+          // Q_t is free once the last S MMA of the previous item that read it is done
+          if (qc[t] && !wait(&q_empty[t], (qc[t] - 1) & 1)) { ok = false; break; }
+          unsigned char* sQ = smem + C::OFF_Q + t * C::Q_BYTES;
+          mbar_arrive_expect_tx(&q_full[t], C::Q_BYTES);
 #pragma unroll
-        for (int db = 0; db < C::DB; ++db) tma_load_4d(sK + db * BN * 128, &tmK, db * 64, j * BN, kvh, b, &k_full[st]);
-        issued = j + 1;
+          for (int db = 0; db < C::DB; ++db)
+            tma_load_4d(sQ + db * BM * 128, &tmQ, db * 64, it.q0[t], it.h[t], it.b, &q_full[t]);
+          ++qc[t];
+        }
+        for (int j = 0; ok && j < it.L; ++j, ++gk) {
+          const uint32_t st = gk % C::NSK;
+          if (gk >= C::NSK && !wait(&k_empty[st], ((gk / C::NSK) - 1) & 1)) { ok = false; break; }
+          unsigned char* sK = smem + C::OFF_K + st * C::KV_BYTES;
+          mbar_arrive_expect_tx(&k_full[st], C::KV_BYTES);
+#pragma unroll
+          for (int db = 0; db < C::DB; ++db)
+            tma_load_4d(sK + db * BN * 128, &tmK, db * 64, j * BN, it.kvh, it.b, &k_full[st]);
+        }
       }
       if (*abort_flag) {  // drain loads still in flight into this CTA's shared memory
-        mbar_wait(q_full, 0);
-        for (int j = max(0, issued - C::NSK); j < issued; ++j) mbar_wait(&k_full[j % C::NSK], (j / C::NSK) & 1);
+        for (int t = 0; t < kSlots; ++t)
+          if (qc[t]) mbar_wait(&q_full[t], (qc[t] - 1) & 1);
+        for (uint32_t g = gk > C::NSK ? gk - C::NSK : 0; g < gk; ++g) mbar_wait(&k_full[g % C::NSK], (g / C::NSK) & 1);
       }
     } else if (lane == 1) {
-      int issued = 0;
-      for (int j = 0; j < n_kv; ++j) {
-        const int st = j % C::NSV;
-        if (j >= C::NSV && !wait(&v_empty[st], ((j / C::NSV) - 1) & 1)) break;
-        unsigned char* sV = smem + C::OFF_V + st * C::KV_BYTES;
-        mbar_arrive_expect_tx(&v_full[st], C::KV_BYTES);
+      uint32_t gv = 0;
+      bool ok = true;
+      for (int i = blockIdx.x; ok && i < p.n_items; i += gridDim.x) {
+        const Item it = decode_item(p, i, BN);
+        for (int j = 0; j < it.L; ++j, ++gv) {
+          const uint32_t st = gv % C::NSV;
+          if (gv >= C::NSV && !wait(&v_empty[st], ((gv / C::NSV) - 1) & 1)) { ok = false; break; }
+          unsigned char* sV = smem + C::OFF_V + st * C::KV_BYTES;
+          mbar_arrive_expect_tx(&v_full[st], C::KV_BYTES);
 #pragma unroll
-        for (int db = 0; db < C::DB; ++db) tma_load_4d(sV + db * BN * 128, &tmV, db * 64, j * BN, kvh, b, &v_full[st]);
-        issued = j + 1;
+          for (int db = 0; db < C::DB; ++db)
+            tma_load_4d(sV + db * BN * 128, &tmV, db * 64, j * BN, it.kvh, it.b, &v_full[st]);
+        }
       }
       if (*abort_flag) {
-        for (int j = max(0, issued - C::NSV); j < issued; ++j) mbar_wait(&v_full[j % C::NSV], (j / C::NSV) & 1);
+        for (uint32_t g = gv > C::NSV ? gv - C::NSV : 0; g < gv; ++g) mbar_wait(&v_full[g % C::NSV], (g / C::NSV) & 1);
       }
     }
-  } else if (warp == 5) {
+  } else if (warp == kMmaWarp) {
     // ========================= MMA issuer =========================
     // The whole warp runs the loop (descriptors stay warp-uniform); one
-    // elected lane issues each MMA and commit.
-    const uint32_t sQ = smem_u32(smem + C::OFF_Q);
-    bool ok = wwait(q_full, 0);
-    tc_fence_after();
-    for (int j = 0; ok && j <= n_kv; ++j) {
-      if (j < n_kv) {
-        const int st = j % C::NSK, sb = j % C::NSB;
-        if (!wwait(&k_full[st], (j / C::NSK) & 1)) break;
-        if (j >= C::NSB && !wwait(&s_empty[sb], ((j / C::NSB) - 1) & 1)) break;
-        tc_fence_after();
-        const uint32_t sK = smem_u32(smem + C::OFF_K + st * C::KV_BYTES);
-        const bool leader = elect_one();
+    // elected lane issues each MMA and commit.  Per key tile j: S_0,j and
+    // S_1,j, then P.V of tile j-1 for both slots, so S of the next tile is
+    // ready when a softmax warpgroup finishes the current one.
+    uint32_t gk = 0, gv = 0, qf[kSlots] = {0, 0}, sc[kSlots] = {0, 0}, pc[kSlots] = {0, 0};
+    bool ok = true;
+    for (int i = blockIdx.x; ok && i < p.n_items; i += gridDim.x) {
+      const Item it = decode_item(p, i, BN);
+      for (int j = 0; ok && j <= it.L; ++j) {
+        if (j < it.L) {
+          const uint32_t st = gk % C::NSK;
+          if (!wwait(&k_full[st], (gk / C::NSK) & 1)) { ok = false; break; }
+          const uint32_t sK = smem_u32(smem + C::OFF_K + st * C::KV_BYTES);
 #pragma unroll
-        for (int k = 0; k < D / 16; ++k) {
-          const uint32_t off = (k >> 2) * (BM * 128) + (k & 3) * 32;
-          const uint32_t offk = (k >> 2) * (BN * 128) + (k & 3) * 32;
-          const uint64_t da = desc_sw128(sQ + off, 16, 1024), db = desc_sw128(sK + offk, 16, 1024);
-          if (leader) mma_f16(tmem + sb * BN, da, db, IDESC_S, k > 0);
-        }
-        if (leader) {
-          mma_commit(&s_full[sb]);
-          mma_commit(&k_empty[st]);
-        }
-        __syncwarp();
-      }
-      if (j >= 1) {
-        const int i = j - 1, pb = i % C::NP, st = i % C::NSV;
-        if (!wwait(&p_full[pb], (i / C::NP) & 1)) break;
-        if (!wwait(&v_full[st], (i / C::NSV) & 1)) break;
-        tc_fence_after();
-        const uint32_t sP = smem_u32(smem + C::OFF_P + pb * C::P_BYTES);
-        const uint32_t sV = smem_u32(smem + C::OFF_V + st * C::KV_BYTES);
-        const bool leader = elect_one();
+          for (int t = 0; t < kSlots; ++t) {
+            if (j >= it.nkv[t]) continue;
+            if (j == 0 && !wwait(&q_full[t], qf[t]++ & 1)) { ok = false; break; }
+            if (sc[t] && !wwait(&s_empty[t], (sc[t] - 1) & 1)) { ok = false; break; }
+            tc_fence_after();
+            const uint32_t sQ = smem_u32(smem + C::OFF_Q + t * C::Q_BYTES);
+            const bool leader = elect_one();
 #pragma unroll
-        for (int k = 0; k < BN / 16; ++k) {
-          const uint32_t offp = (k >> 2) * (BM * 128) + (k & 3) * 32;
-          const uint64_t da = desc_sw128(sP + offp, 16, 1024), db = desc_sw128(sV + k * 2048, BN * 128, 1024);
-          if (leader) mma_f16(tmem + C::COL_O, da, db, IDESC_PV, (i > 0 || k > 0) ? 1u : 0u);
+            for (int k = 0; k < D / 16; ++k) {
+              const uint32_t offq = (k >> 2) * (BM * 128) + (k & 3) * 32;
+              const uint32_t offk = (k >> 2) * (BN * 128) + (k & 3) * 32;
+              const uint64_t da = desc_sw128(sQ + offq, 16, 1024), db = desc_sw128(sK + offk, 16, 1024);
+              if (leader) mma_f16(tmem + C::COL_S + t * BN, da, db, IDESC_S, k > 0);
+            }
+            if (leader) {
+              mma_commit(&s_full[t]);
+              if (j == it.nkv[t] - 1) mma_commit(&q_empty[t]);
+            }
+            __syncwarp();
+            ++sc[t];
+          }
+          if (!ok) break;
+          if (elect_one()) mma_commit(&k_empty[st]);
+          __syncwarp();
+          ++gk;
         }
-        if (leader) {
-          mma_commit(o_done);
-          mma_commit(&p_empty[pb]);
-          mma_commit(&v_empty[st]);
+        if (j >= 1) {
+          const int jj = j - 1;
+          const uint32_t st = gv % C::NSV;
+          if (!wwait(&v_full[st], (gv / C::NSV) & 1)) { ok = false; break; }
+          const uint32_t sV = smem_u32(smem + C::OFF_V + st * C::KV_BYTES);
+#pragma unroll
+          for (int t = 0; t < kSlots; ++t) {
+            if (jj >= it.nkv[t]) continue;
+            if (!wwait(&p_full[t], pc[t] & 1)) { ok = false; break; }
+            tc_fence_after();
+            const bool leader = elect_one();
+#pragma unroll
+            for (int k = 0; k < BN / 16; ++k) {
+              const uint64_t db = desc_sw128(sV + k * 2048, BN * 128, 1024);
+              if (leader)
+                mma_f16_ts(tmem + C::COL_O + t * D, tmem + C::COL_P + t * (BN / 2) + k * 8, db, IDESC_PV,
+                           (jj > 0 || k > 0) ? 1u : 0u);
+            }
+            if (leader) mma_commit(&pv_done[t]);
+            __syncwarp();
+            ++pc[t];
+          }
+          if (!ok) break;
+          if (elect_one()) mma_commit(&v_empty[st]);
+          __syncwarp();
+          ++gv;
         }
-        __syncwarp();
       }
     }
     // every MMA issued by this warp has finished before the CTA can exit
@@ -363,138 +473,157 @@ __global__ void __launch_bounds__(kThreads, (Cfg<D, BN>::CTAS_PER_SM))
     __syncwarp();
     mbar_wait(mma_idle, 0);
   } else {
-    // ========================= softmax warpgroup =========================
-    const int t = threadIdx.x;  // 0..127: row t of the tile, TMEM lane t
-    const int row = q0 + t;
-    const uint32_t lane_addr = (uint32_t)(warp * 32) << 16;
-    float m_use = -INFINITY, l = 0.f;
-    int pv_seen = 0;
+    // ========================= softmax warpgroups =========================
+    const int t = warp >> 2;                   // slot
+    const int r = threadIdx.x & (BM - 1);      // row in the tile = TMEM lane
+    const uint32_t lane_addr = (uint32_t)((warp & 3) * 32) << 16;
+    const uint32_t tS = tmem + lane_addr + C::COL_S + t * BN;
+    const uint32_t tO = tmem + lane_addr + C::COL_O + t * D;
+    const uint32_t tP = tmem + lane_addr + C::COL_P + t * (BN / 2);
+    uint32_t sc = 0, pc = 0;
     bool ok = true;
-    for (int j = 0; j < n_kv; ++j) {
-      const int sb = j % C::NSB, pb = j % C::NP;
-      if (!wait(&s_full[sb], (j / C::NSB) & 1)) { ok = false; break; }
-      tc_fence_after();
-      float x[BN];
-      {
-        uint32_t r[BN / 32][32];
+    for (int i = blockIdx.x; ok && i < p.n_items; i += gridDim.x) {
+      const Item it = decode_item(p, i, BN);
+      // slot fields selected without dynamic indexing (keeps Item in registers)
+      const int q0 = t ? it.q0[1] : it.q0[0], hq = t ? it.h[1] : it.h[0], nkv = t ? it.nkv[1] : it.nkv[0];
+      const int row = q0 + r;
+      T* orow = static_cast<T*>(p.o) + (int64_t)it.b * p.o_sb + (int64_t)hq * p.o_sh + (int64_t)row * p.o_ss;
+      if (!nkv) {  // slot entirely past the sequence (var-len padding): zeros
+        if (row < p.S) {
 #pragma unroll
-        for (int c = 0; c < BN / 32; ++c) tmem_ld32(tmem + lane_addr + sb * BN + c * 32, r[c]);
-        tmem_wait_ld();
-#pragma unroll
-        for (int c = 0; c < BN / 32; ++c)
-#pragma unroll
-          for (int e = 0; e < 32; ++e) x[c * 32 + e] = __uint_as_float(r[c][e]);
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&s_empty[sb]);
-      // masks only where a key tile reaches past the tile's first row (causal
-      // diagonal) or past S
-      if ((p.causal && (j + 1) * BN - 1 > q0) || (j + 1) * BN > p.S) {
-        const int lim = min(p.causal ? row : p.S - 1, p.S - 1) - j * BN;  // last visible column
-#pragma unroll
-        for (int c = 0; c < BN; ++c) x[c] = c > lim ? -INFINITY : x[c];
-      }
-      // row max of the raw scores (scale > 0), 8 independent chains
-      float mx8[8];
-#pragma unroll
-      for (int e = 0; e < 8; ++e) mx8[e] = x[e];
-#pragma unroll
-      for (int c = 8; c < BN; ++c) mx8[c & 7] = fmaxf(mx8[c & 7], x[c]);
-      const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
-                             fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7]))) * p.scale_log2;
-      const float m_new = fmaxf(m_use, mx);
-      const bool need = m_new > m_use + kRescaleThreshold || (m_use == -INFINITY && m_new != -INFINITY);
-      float alpha = 1.f;
-      if (need) {
-        alpha = fast_exp2(m_use - m_new);
-        m_use = m_new;
-      }
-      const float m_sub = m_use == -INFINITY ? 0.f : m_use;
-      // P = 2^(s*scale - m) in the input dtype, packed in registers first so the
-      // exponentials do not wait for the previous P.V to release the P tile
-      float rs8[8];
-#pragma unroll
-      for (int e = 0; e < 8; ++e) rs8[e] = 0.f;
-      uint32_t pk[BN / 2];
-#pragma unroll
-      for (int ch = 0; ch < BN / 8; ++ch) {
-        float pv[8];
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          pv[e] = fast_exp2(fmaf(x[ch * 8 + e], p.scale_log2, -m_sub));
-          rs8[e] += pv[e];
+          for (int c = 0; c < D; c += 8) *reinterpret_cast<uint4*>(orow + c) = make_uint4(0, 0, 0, 0);
         }
-#pragma unroll
-        for (int e = 0; e < 4; ++e) pk[ch * 4 + e] = pack_p<T>(pv[2 * e], pv[2 * e + 1]);
+        continue;
       }
-      if (j >= C::NP && !wait(&p_empty[pb], ((j / C::NP) - 1) & 1)) { ok = false; break; }
-      unsigned char* sP = smem + C::OFF_P + pb * C::P_BYTES;
+      float m_use = -INFINITY, l = 0.f;
+      for (int j = 0; j < nkv; ++j) {
+        if (!wait(&s_full[t], sc & 1)) { ok = false; break; }
+        ++sc;
+        tc_fence_after();
+        float x[BN];
+        {
+          uint32_t rr[BN / 32][32];
 #pragma unroll
-      for (int ch = 0; ch < BN / 8; ++ch) {
-        const int kb = ch >> 3, cin = ch & 7;
-        *reinterpret_cast<uint4*>(sP + kb * (BM * 128) + t * 128 + ((cin ^ (t & 7)) << 4)) =
-            make_uint4(pk[ch * 4 + 0], pk[ch * 4 + 1], pk[ch * 4 + 2], pk[ch * 4 + 3]);
-      }
-      const float rs = ((rs8[0] + rs8[1]) + (rs8[2] + rs8[3])) + ((rs8[4] + rs8[5]) + (rs8[6] + rs8[7]));
-      l = l * alpha + rs;
-      // O must see PV_{j-1} finished before it is rescaled or before PV_j is queued
-      if (j >= 1) {
-        while (pv_seen < j) {
-          if (!wait(o_done, pv_seen & 1)) { ok = false; break; }
-          ++pv_seen;
+          for (int c = 0; c < BN / 32; ++c) tmem_ld32(tS + c * 32, rr[c]);
+          tmem_wait_ld();
+#pragma unroll
+          for (int c = 0; c < BN / 32; ++c)
+#pragma unroll
+            for (int e = 0; e < 32; ++e) x[c * 32 + e] = __uint_as_float(rr[c][e]);
         }
-        if (!ok) break;
-        if (__any_sync(0xffffffffu, need)) {
-          tc_fence_after();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s_empty[t]);
+        // masks only where a key tile reaches past the tile's first row (causal
+        // diagonal) or past S
+        const bool masked = (p.causal && (j + 1) * BN - 1 > q0) || (j + 1) * BN > p.S;
+        if (masked) {
+          const int lim = min(p.causal ? row : p.S - 1, p.S - 1) - j * BN;  // last visible column
 #pragma unroll
-          for (int c = 0; c < D / 32; ++c) {
-            uint32_t r[32];
-            tmem_ld32(tmem + lane_addr + C::COL_O + c * 32, r);
-            tmem_wait_ld();
+          for (int c = 0; c < BN; ++c) x[c] = c > lim ? -INFINITY : x[c];
+        }
+        // row max of the raw scores (scale > 0): 4 chains of 3-input max
+        float mx;
+        {
+          float a0 = fmaxf(x[0], x[4]), a1 = fmaxf(x[1], x[5]), a2 = fmaxf(x[2], x[6]), a3 = fmaxf(x[3], x[7]);
 #pragma unroll
-            for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * alpha);
-            tmem_st32(tmem + lane_addr + C::COL_O + c * 32, r);
+          for (int c = 8; c < BN; c += 8) {
+            a0 = max3f(a0, x[c + 0], x[c + 1]);
+            a1 = max3f(a1, x[c + 2], x[c + 3]);
+            a2 = max3f(a2, x[c + 4], x[c + 5]);
+            a3 = max3f(a3, x[c + 6], x[c + 7]);
           }
-          tmem_wait_st();
+          mx = max3f(a0, a1, fmaxf(a2, a3)) * p.scale_log2;
+        }
+        const float m_new = fmaxf(m_use, mx);
+        const bool need = m_new > m_use + kRescaleThreshold || (m_use == -INFINITY && m_new != -INFINITY);
+        float alpha = 1.f;
+        if (need) {
+          alpha = fast_exp2(m_use - m_new);
+          m_use = m_new;
+        }
+        const float m_sub = m_use == -INFINITY ? 0.f : m_use;
+        // P = 2^(s*scale - m), packed to the input dtype
+        const float2 sl2 = make_float2(p.scale_log2, p.scale_log2), nm2 = make_float2(-m_sub, -m_sub);
+        float2 rs2[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) rs2[e] = make_float2(0.f, 0.f);
+        uint32_t pk[BN / 64][32];
+        if (masked || C::POLY == 0) {
+#pragma unroll
+          for (int e = 0; e < BN / 2; ++e) {
+            const float2 v = ffma2(make_float2(x[2 * e], x[2 * e + 1]), sl2, nm2);
+            const float2 ev = make_float2(fast_exp2(v.x), fast_exp2(v.y));
+            rs2[e & 3] = __fadd2_rn(rs2[e & 3], ev);
+            pk[e >> 5][e & 31] = pack_p<T>(ev.x, ev.y);
+          }
+        } else {
+#pragma unroll
+          for (int e = 0; e < BN / 2; ++e) {
+            const float2 v = ffma2(make_float2(x[2 * e], x[2 * e + 1]), sl2, nm2);
+            const float2 ev = (e / 4) < C::POLY ? exp2_poly2(v) : make_float2(fast_exp2(v.x), fast_exp2(v.y));
+            rs2[e & 3] = __fadd2_rn(rs2[e & 3], ev);
+            pk[e >> 5][e & 31] = pack_p<T>(ev.x, ev.y);
+          }
+        }
+        const float2 rs01 = __fadd2_rn(rs2[0], rs2[1]), rs23 = __fadd2_rn(rs2[2], rs2[3]);
+        const float2 rsum = __fadd2_rn(rs01, rs23);
+        l = l * alpha + (rsum.x + rsum.y);
+        // P_t and O_t are free once the previous P.V of this slot is done
+        if (j >= 1) {
+          if (!wait(&pv_done[t], pc & 1)) { ok = false; break; }
+          ++pc;
+          tc_fence_after();
+          if (__any_sync(0xffffffffu, need)) {
+#pragma unroll
+            for (int c = 0; c < D / 32; ++c) {
+              uint32_t rr[32];
+              tmem_ld32(tO + c * 32, rr);
+              tmem_wait_ld();
+#pragma unroll
+              for (int e = 0; e < 32; ++e) rr[e] = __float_as_uint(__uint_as_float(rr[e]) * alpha);
+              tmem_st32(tO + c * 32, rr);
+            }
+          }
+        }
+#pragma unroll
+        for (int c = 0; c < BN / 64; ++c) tmem_st32(tP + c * 32, pk[c]);
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&p_full[t]);
+      }
+      if (!ok) break;
+      // ---- epilogue: O / l for valid rows, zeros for var-len padding rows
+      if (!wait(&pv_done[t], pc & 1)) { ok = false; break; }
+      ++pc;
+      tc_fence_after();
+      const float inv = (l > 0.f && row < it.seq_len) ? 1.f / l : 0.f;
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t rr[32];
+        tmem_ld32(tO + c * 32, rr);
+        tmem_wait_ld();
+        if (row < p.S) {
+#pragma unroll
+          for (int e = 0; e < 32; e += 8) {
+            uint4 w;
+            w.x = Elem<T>::pack2(__uint_as_float(rr[e + 0]) * inv, __uint_as_float(rr[e + 1]) * inv);
+            w.y = Elem<T>::pack2(__uint_as_float(rr[e + 2]) * inv, __uint_as_float(rr[e + 3]) * inv);
+            w.z = Elem<T>::pack2(__uint_as_float(rr[e + 4]) * inv, __uint_as_float(rr[e + 5]) * inv);
+            w.w = Elem<T>::pack2(__uint_as_float(rr[e + 6]) * inv, __uint_as_float(rr[e + 7]) * inv);
+            *reinterpret_cast<uint4*>(orow + c * 32 + e) = w;
+          }
         }
       }
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      // O_t is overwritten by the next item's first P.V only after this
+      // warpgroup's p_full arrive, which follows these loads in program order
       tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full[pb]);
-    }
-    // ---- epilogue: O / l for valid rows, zeros for var-len padding rows
-    if (ok) {
-      while (pv_seen < n_kv) {
-        if (!wait(o_done, pv_seen & 1)) { ok = false; break; }
-        ++pv_seen;
-      }
-    }
-    T* orow = static_cast<T*>(p.o) + (int64_t)b * p.o_sb + (int64_t)h * p.o_sh + (int64_t)row * p.o_ss;
-    const float inv = (ok && l > 0.f && row < seq_len) ? 1.f / l : 0.f;
-    tc_fence_after();
-#pragma unroll
-    for (int c = 0; c < D / 32; ++c) {
-      uint32_t r[32];
-      tmem_ld32(tmem + lane_addr + C::COL_O + c * 32, r);
-      tmem_wait_ld();
-      if (row < p.S) {
-#pragma unroll
-        for (int e = 0; e < 32; e += 8) {
-          uint4 w;
-          w.x = Elem<T>::pack2(__uint_as_float(r[e + 0]) * inv, __uint_as_float(r[e + 1]) * inv);
-          w.y = Elem<T>::pack2(__uint_as_float(r[e + 2]) * inv, __uint_as_float(r[e + 3]) * inv);
-          w.z = Elem<T>::pack2(__uint_as_float(r[e + 4]) * inv, __uint_as_float(r[e + 5]) * inv);
-          w.w = Elem<T>::pack2(__uint_as_float(r[e + 6]) * inv, __uint_as_float(r[e + 7]) * inv);
-          *reinterpret_cast<uint4*>(orow + c * 32 + e) = w;
-        }
-      }
     }
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == kMmaWarp) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(C::TMEM_COLS));
   }
@@ -532,14 +661,26 @@ int make_map(CUtensorMap* m, const void* base, int dtype, int B, int H, int S, i
   return AKT_OK;
 }
 
-template <typename T, int D, int BN>
+int sm_count() {
+  static int counts[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (!counts[dev]) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    counts[dev] = n;
+  }
+  return counts[dev];
+}
+
+template <typename T, int D>
 int launch_prefill(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const PrefillParams& p,
                    cudaStream_t st) {
-  auto kern = prefill_fwd_kernel<T, D, BN>;
-  const int smem = (int)Cfg<D, BN>::SMEM;
+  auto kern = prefill_fwd_kernel<T, D>;
+  const int smem = (int)Cfg<D>::SMEM;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return set_error(AKT_ERR_CUDA, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
-  dim3 grid(p.n_q_tiles, p.Hq, p.B);
+  const int grid = std::min(p.n_items, sm_count());  // persistent: one CTA per SM
   {
     ProfileScope prof(st);
     kern<<<grid, kThreads, smem, st>>>(mq, mk, mv, p);
@@ -550,18 +691,6 @@ int launch_prefill(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorM
 }
 
 bool al16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; }
-
-// keys per tile: AKT_PREFILL_BN (64 or 128) overrides the default, read once
-int prefill_key_tile(int D) {
-  static int forced = -1;
-  if (forced < 0) {
-    const char* v = getenv("AKT_PREFILL_BN");
-    forced = v ? atoi(v) : 0;
-    if (forced != 64 && forced != 128) forced = 0;
-  }
-  if (forced) return forced;
-  return D == 64 ? 64 : 128;
-}
 
 }  // namespace
 }  // namespace akt
@@ -587,7 +716,7 @@ extern "C" int akt_prefill(const akt_prefill_args* a, void* stream) {
   if (!(a->softmax_scale > 0.f) || a->softmax_scale == INFINITY)
     return set_error(AKT_ERR_UNSUPPORTED, "prefill: softmax_scale must be positive and finite");
   if (a->batch == 0 || a->seq_len == 0) return AKT_OK;
-  const int bn = prefill_key_tile(a->head_dim);
+  const int bn = a->head_dim == 64 ? Cfg<64>::BN : Cfg<128>::BN;
   CUtensorMap mq, mk, mv;
   int rc = make_map(&mq, a->q, a->dtype, a->batch, a->num_qo_heads, a->seq_len, a->head_dim, a->q_stride_batch,
                     a->q_stride_head, a->q_stride_token, BM);
@@ -603,17 +732,16 @@ extern "C" int akt_prefill(const akt_prefill_args* a, void* stream) {
   p.B = a->batch; p.Hq = a->num_qo_heads; p.Hkv = a->num_kv_heads; p.S = a->seq_len;
   p.group = p.Hq / p.Hkv;
   p.n_q_tiles = (a->seq_len + BM - 1) / BM;
+  p.pair_heads = p.group % 2 == 0 ? 1 : 0;
+  const int64_t items = p.pair_heads ? (int64_t)p.n_q_tiles * p.B * (p.Hq / 2)
+                                     : (int64_t)((p.n_q_tiles + 1) / 2) * p.B * p.Hq;
+  if (items > INT32_MAX) return set_error(AKT_ERR_UNSUPPORTED, "prefill: too many query tiles");
+  p.n_items = (int)items;
   p.causal = a->causal ? 1 : 0;
   p.scale_log2 = a->softmax_scale * kLog2e;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (a->dtype == AKT_FLOAT16) {
-    if (a->head_dim == 64)
-      return bn == 64 ? launch_prefill<__half, 64, 64>(mq, mk, mv, p, st) : launch_prefill<__half, 64, 128>(mq, mk, mv, p, st);
-    return bn == 64 ? launch_prefill<__half, 128, 64>(mq, mk, mv, p, st) : launch_prefill<__half, 128, 128>(mq, mk, mv, p, st);
-  }
-  if (a->head_dim == 64)
-    return bn == 64 ? launch_prefill<__nv_bfloat16, 64, 64>(mq, mk, mv, p, st)
-                    : launch_prefill<__nv_bfloat16, 64, 128>(mq, mk, mv, p, st);
-  return bn == 64 ? launch_prefill<__nv_bfloat16, 128, 64>(mq, mk, mv, p, st)
-                  : launch_prefill<__nv_bfloat16, 128, 128>(mq, mk, mv, p, st);
+  if (a->dtype == AKT_FLOAT16)
+    return a->head_dim == 64 ? launch_prefill<__half, 64>(mq, mk, mv, p, st) : launch_prefill<__half, 128>(mq, mk, mv, p, st);
+  return a->head_dim == 64 ? launch_prefill<__nv_bfloat16, 64>(mq, mk, mv, p, st)
+                           : launch_prefill<__nv_bfloat16, 128>(mq, mk, mv, p, st);
 }
