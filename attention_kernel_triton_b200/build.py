@@ -21,8 +21,16 @@ BUILD = os.path.join(ROOT, "_build")
 LIB = os.path.join(PKG, "libakt.so")
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
-NVCC_FLAGS = ARCH + ["-O3", "-std=c++17", "-lineinfo", "-rdc=true", "-Xcompiler", "-fPIC",
+NVCC_FLAGS = ARCH + ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC",
                      "-I" + os.path.join(ROOT, "include"), "--expt-relaxed-constexpr"]
+# Files compiled as whole-program device code: ptxas ignores setmaxnreg in
+# relocatable device code, and the prefill kernel's warpgroup register split
+# depends on it.  They reference no device symbol of another file.
+WHOLE_PROGRAM = {"prefill.cu"}
+
+
+def flags_for(src: str):
+    return NVCC_FLAGS + ([] if os.path.basename(src) in WHOLE_PROGRAM else ["-rdc=true"])
 
 
 def nvcc() -> str:
@@ -50,7 +58,7 @@ def build(verbose: bool = False, force: bool = False) -> str:
         o = os.path.join(BUILD, os.path.basename(s)[:-3] + ".o")
         objs.append(o)
         if force or _needs(o, [s] + headers):
-            jobs.append([cc] + NVCC_FLAGS + ["-c", s, "-o", o])
+            jobs.append([cc] + flags_for(s) + ["-c", s, "-o", o])
 
     def run(cmd):
         if verbose:

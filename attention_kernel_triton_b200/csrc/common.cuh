@@ -15,7 +15,18 @@ namespace akt {
 // device status word: first error recorded by any kernel of this library.
 // Kernels never trap; they record a code here and skip the offending access.
 // ---------------------------------------------------------------------------
+// Files built as whole-program device code (without -rdc, so that ptxas
+// applies setmaxnreg register budgets) keep their own word, which the host
+// status functions read and clear together with the shared one.
+#ifdef AKT_WHOLE_PROGRAM
+namespace {
+__device__ unsigned int g_device_status_local = 0;
+}
+#define AKT_STATUS_WORD g_device_status_local
+#else
 extern __device__ unsigned int g_device_status;
+#define AKT_STATUS_WORD g_device_status
+#endif
 
 enum DeviceStatus : unsigned int {
   kStatusOk = 0,
@@ -26,7 +37,7 @@ enum DeviceStatus : unsigned int {
 };
 
 __device__ __forceinline__ void record_status(unsigned int code) {
-  atomicCAS(&g_device_status, 0u, code);
+  atomicCAS(&AKT_STATUS_WORD, 0u, code);
 }
 
 // ---------------------------------------------------------------------------

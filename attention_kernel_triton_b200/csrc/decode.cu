@@ -36,6 +36,10 @@ namespace akt {
 
 __device__ unsigned int g_device_status = 0;
 
+// status word of the prefill kernels (prefill.cu is whole-program device code)
+cudaError_t prefill_status_read(unsigned int* v);
+cudaError_t prefill_status_clear();
+
 constexpr int kProducerWarps = 1;
 constexpr int kConsumerWarps = 4;
 constexpr int kDecodeThreads = 32 * (kProducerWarps + kConsumerWarps);
@@ -512,8 +516,10 @@ int akt_device_status(int device, unsigned int* status_out) {
   cudaGetDevice(&prev);
   cudaError_t e = cudaSetDevice(device);
   if (e == cudaSuccess) e = cudaDeviceSynchronize();
-  unsigned int v = 0;
+  unsigned int v = 0, vp = 0;
   if (e == cudaSuccess) e = cudaMemcpyFromSymbol(&v, g_device_status, sizeof(v));
+  if (e == cudaSuccess) e = prefill_status_read(&vp);
+  if (v == 0) v = vp;
   cudaSetDevice(prev);
   if (e != cudaSuccess) return set_error(AKT_ERR_CUDA, cudaGetErrorString(e));
   if (status_out) *status_out = v;
@@ -526,6 +532,7 @@ int akt_clear_device_status(int device) {
   cudaError_t e = cudaSetDevice(device);
   unsigned int z = 0;
   if (e == cudaSuccess) e = cudaMemcpyToSymbol(g_device_status, &z, sizeof(z));
+  if (e == cudaSuccess) e = prefill_status_clear();
   if (e == cudaSuccess) e = cudaDeviceSynchronize();
   cudaSetDevice(prev);
   if (e != cudaSuccess) return set_error(AKT_ERR_CUDA, cudaGetErrorString(e));

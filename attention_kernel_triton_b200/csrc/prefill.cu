@@ -16,14 +16,17 @@
 //              i = TMEM lane i; reads S with tcgen05.ld, writes P (input
 //              dtype) back to TMEM with tcgen05.st, rescales O in TMEM when
 //              its running max moves, and writes the normalised output.
-//   warp 8     TMA producer: lane 0 loads Q and the K ring, lane 1 the V ring.
-//   warp 9     TMEM allocator and MMA issuer (one elected lane):
+//   warp 8     TMA producer of Q and the K ring; warp 10 of the V ring.
+//   warp 9     TMEM allocator; its lane 0 issues slot 0's MMAs, lane 0 of
+//              warp 11 those of slot 1:
 //              S_t = Q_t K_j^T (M=128, N=BN, K=D; A and B in shared memory)
 //              O_t += P_t V_j   (M=128, N=D,  K=BN; A = P in TMEM, B = V)
 // TMEM (512 columns): S[2] (BN each), O[2] (D each), P[2] (BN/2 each, two
 // 16-bit values per column).  With S and P apart, S for key tile j+1 is
 // computed while the softmax still works on tile j; the only per-tile wait
 // of a softmax warpgroup is for its previous P.V before it overwrites P.
+// The third warpgroup's spare registers go to the softmax warpgroups
+// (setmaxnreg).
 //
 // The running max used for exponentiation only moves when the row max grows
 // by more than 8 (log2 units), so O is rescaled rarely (P <= 2^8 stays exact
@@ -31,6 +34,9 @@
 // tiles without masking a share of the exponentials is evaluated on the FMA
 // pipe by a polynomial (exp2_poly2) instead of the MUFU unit, whose 16
 // results per clock per SM would otherwise bound a head_dim-64 kernel.
+// Built without -rdc (whole-program device code): with relocatable device
+// code ptxas ignores setmaxnreg, and the softmax warpgroups need its budget.
+#define AKT_WHOLE_PROGRAM 1
 #include "common.cuh"
 #include "profile.cuh"
 
@@ -51,9 +57,18 @@ namespace {
 
 constexpr int BM = 128;            // query rows per slot
 constexpr int kSlots = 2;          // query tiles per work item
-constexpr int kThreads = 320;      // 2 softmax warpgroups + producer warp + MMA warp
-constexpr int kLoadWarp = 8;
+constexpr int kThreads = 384;      // 2 softmax warpgroups + a warpgroup holding the producer and MMA warps
+constexpr int kLoadWarp = 8;       // Q and the K ring
 constexpr int kMmaWarp = 9;
+constexpr int kLoadVWarp = 10;     // the V ring (its own warp: two waiting lanes of one warp stall each other)
+constexpr int kMmaWarp1 = 11;      // MMA issuer of slot 1 (slot 0: kMmaWarp)
+// Register split: the kernel is compiled for 168 registers per thread (3 warps
+// per SM sub-partition); the producer/MMA warpgroup gives registers back and
+// the softmax warpgroups take them: 2*128*216 + 128*64 <= 384*168.
+constexpr int kLaunchRegs = 168;
+constexpr int kSoftmaxRegs = 216;
+constexpr int kControlRegs = 64;
+static_assert(2 * 128 * kSoftmaxRegs + 128 * kControlRegs <= kThreads * kLaunchRegs, "register split");
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 
 // 8-element chunks of a row evaluated by the FMA-pipe polynomial (of BN/8) on
@@ -64,8 +79,8 @@ constexpr float kRescaleThreshold = 8.0f;  // log2 units
 
 // Tile configuration per head_dim D.  Keys per tile BN is chosen so that
 // S[2], O[2] and P[2] fit the 512 TMEM columns of one SM:
-//   D=64 : BN=128 -> 256 + 128 + 128 = 512 columns, smem 32 KB Q + rings
-//   D=128: BN=64  -> 128 + 256 +  64 = 448 columns, smem 64 KB Q + rings
+//   D=64 : BN=128 -> 256 + 128 + 128 = 512 columns; smem 64 KB Q + 3-stage K, V rings = 160 KB
+//   D=128: BN=64  -> 128 + 256 +  64 = 448 columns; smem 128 KB Q + 2-stage rings = 192 KB
 template <int D>
 struct Cfg {
   static constexpr int BN = D == 64 ? 128 : 64;
@@ -75,16 +90,23 @@ struct Cfg {
   static constexpr int COL_P = 2 * BN + 2 * D;            // + slot * BN / 2
   static constexpr int TMEM_COLS = 512;
   static_assert(COL_P + BN <= TMEM_COLS, "TMEM budget");
-  static constexpr int NSK = 3, NSV = 3;                  // K / V ring stages
+  static constexpr int NQ = 2;                            // Q buffers per slot (next item's Q loads early)
+  static constexpr int NSK = D == 64 ? 3 : 2, NSV = NSK;  // K / V ring stages
   static constexpr int CHUNKS = BN / 8;
   static constexpr int POLY = AKT_PREFILL_POLY_CHUNKS < CHUNKS ? AKT_PREFILL_POLY_CHUNKS : CHUNKS;
   static constexpr uint32_t Q_BYTES = BM * D * 2;         // one slot
   static constexpr uint32_t KV_BYTES = BN * D * 2;        // one K or V tile
   static constexpr uint32_t OFF_Q = 0;
-  static constexpr uint32_t OFF_K = OFF_Q + kSlots * Q_BYTES;
+  static constexpr uint32_t OFF_K = OFF_Q + kSlots * NQ * Q_BYTES;
   static constexpr uint32_t OFF_V = OFF_K + NSK * KV_BYTES;
   static constexpr uint32_t OFF_BAR = OFF_V + NSV * KV_BYTES;
-  static constexpr uint32_t SMEM = OFF_BAR + 256;         // + barriers (base is 1024-aligned)
+  // mbarriers: q_full/q_empty [slot][NQ], k and v full/empty rings, s_full,
+  // s_empty, p_full, pv_done [slot], mma_idle; then the TMEM address word and
+  // the abort flag
+  static constexpr int N_BARS = 2 * kSlots * NQ + 2 * NSK + 2 * NSV + 4 * kSlots + 1;
+  static constexpr uint32_t BAR_BYTES = (N_BARS * 8 + 8 + 15) / 16 * 16;
+  static constexpr uint32_t SMEM = OFF_BAR + BAR_BYTES;  // base is 1024-aligned
+  static_assert(SMEM <= 227 * 1024, "shared memory budget");
 };
 
 struct PrefillParams {
@@ -220,18 +242,6 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, i
       : "memory");
 }
 
-// one lane of a converged warp (the issuing lane for MMA / TMA / commit)
-__device__ __forceinline__ bool elect_one() {
-  uint32_t pred = 0;
-  asm volatile(
-      "{\n\t.reg .b32 rx;\n\t.reg .pred px;\n\t"
-      "elect.sync rx|px, %1;\n\t"
-      "@px mov.s32 %0, 1;\n\t}"
-      : "+r"(pred)
-      : "r"(0xffffffffu));
-  return pred != 0;
-}
-
 __device__ __forceinline__ float max3f(float a, float b, float c) {
   float r;
   asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
@@ -266,6 +276,47 @@ __device__ __forceinline__ uint32_t pack_p(float a, float b) {
   return Elem<T>::pack2(a, b);
 }
 
+// Normalised output row of one softmax thread: O (D fp32 TMEM columns at tO)
+// times inv, converted to T and stored at orow (null: rows past S, not stored).
+template <typename T, int D>
+__device__ __forceinline__ void write_output(uint32_t tO, T* orow, float inv) {
+#pragma unroll
+  for (int c = 0; c < D / 32; ++c) {
+    uint32_t rr[32];
+    tmem_ld32(tO + c * 32, rr);
+    tmem_wait_ld();
+    if (orow) {
+#pragma unroll
+      for (int e = 0; e < 32; e += 8) {
+        uint4 w;
+        w.x = Elem<T>::pack2(__uint_as_float(rr[e + 0]) * inv, __uint_as_float(rr[e + 1]) * inv);
+        w.y = Elem<T>::pack2(__uint_as_float(rr[e + 2]) * inv, __uint_as_float(rr[e + 3]) * inv);
+        w.z = Elem<T>::pack2(__uint_as_float(rr[e + 4]) * inv, __uint_as_float(rr[e + 5]) * inv);
+        w.w = Elem<T>::pack2(__uint_as_float(rr[e + 6]) * inv, __uint_as_float(rr[e + 7]) * inv);
+        *reinterpret_cast<uint4*>(orow + c * 32 + e) = w;
+      }
+    }
+  }
+}
+
+// Slow path of a bounded mbarrier wait: spins on try_wait; every 256 polls it
+// gives up if another role of the CTA has aborted, or, after kWaitLimitNs,
+// records kStatusWaitTimeout and raises the abort flag itself.
+__device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t it = 1;; ++it) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((it & 255u) == 0u) {
+      if (*abort_flag) return false;
+      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        record_status(kStatusWaitTimeout);
+        *abort_flag = 1;
+        return false;
+      }
+    }
+  }
+}
+
 // -------------------------------------------------------------------------
 // kernel
 // -------------------------------------------------------------------------
@@ -285,16 +336,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     return;
   }
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
-  uint64_t* q_full = bars;                       // [2]
-  uint64_t* q_empty = q_full + kSlots;           // [2]
-  uint64_t* k_full = q_empty + kSlots;           // [NSK]
+  uint64_t* q_full = bars;                       // [slot][NQ]
+  uint64_t* q_empty = q_full + kSlots * C::NQ;   // [slot][NQ]
+  uint64_t* k_full = q_empty + kSlots * C::NQ;   // [NSK]
   uint64_t* k_empty = k_full + C::NSK;           // [NSK]
   uint64_t* v_full = k_empty + C::NSK;           // [NSV]
   uint64_t* v_empty = v_full + C::NSV;           // [NSV]
-  uint64_t* s_full = v_empty + C::NSV;           // [2]
-  uint64_t* s_empty = s_full + kSlots;           // [2]
-  uint64_t* p_full = s_empty + kSlots;           // [2]
-  uint64_t* pv_done = p_full + kSlots;           // [2]
+  uint64_t* s_full = v_empty + C::NSV;           // [slot]
+  uint64_t* s_empty = s_full + kSlots;           // [slot]
+  uint64_t* p_full = s_empty + kSlots;           // [slot]
+  uint64_t* pv_done = p_full + kSlots;           // [slot]
   uint64_t* mma_idle = pv_done + kSlots;         // 1
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_idle + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -303,8 +354,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (threadIdx.x == 0) {
     for (int t = 0; t < kSlots; ++t) {
-      mbar_init(&q_full[t], 1);
-      mbar_init(&q_empty[t], 1);
+      for (int q = 0; q < C::NQ; ++q) {
+        mbar_init(&q_full[t * C::NQ + q], 1);
+        mbar_init(&q_empty[t * C::NQ + q], 1);
+      }
       mbar_init(&s_full[t], 1);
       mbar_init(&s_empty[t], 4);
       mbar_init(&p_full[t], 4);
@@ -312,13 +365,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int s = 0; s < C::NSK; ++s) {
       mbar_init(&k_full[s], 1);
-      mbar_init(&k_empty[s], 1);
+      mbar_init(&k_empty[s], kSlots);  // one commit per slot's MMA issuer
     }
     for (int s = 0; s < C::NSV; ++s) {
       mbar_init(&v_full[s], 1);
-      mbar_init(&v_empty[s], 1);
+      mbar_init(&v_empty[s], kSlots);
     }
-    mbar_init(mma_idle, 1);
+    mbar_init(mma_idle, kSlots);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -332,36 +385,37 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
+  // A completed phase costs one try_wait (~20 cycles); the abort flag and the
+  // time limit are only looked at while spinning, because a shared-memory
+  // load ahead of every try_wait costs ~10x that on the issuing thread.
   auto wait = [&](uint64_t* bar, uint32_t parity) -> bool {
-    if (*abort_flag) return false;
-    if (mbar_wait(bar, parity)) return true;
-    *abort_flag = 1;
-    return false;
-  };
-  // warp-uniform variant for the warp that issues MMAs in lockstep
-  auto wwait = [&](uint64_t* bar, uint32_t parity) -> bool {
-    return __all_sync(0xffffffffu, wait(bar, parity)) != 0;
+    if (mbar_try_wait(bar, parity)) return true;
+    return wait_or_abort(bar, parity, abort_flag);
   };
 
-  if (warp == kLoadWarp) {
+  if (warp >= 8) {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kControlRegs));
+  if (warp == kLoadWarp || warp == kLoadVWarp) {
     // ========================= TMA producers =========================
-    // Phases continue across items: counters are global to the CTA.
-    if (lane == 0) {
-      uint32_t qc[kSlots] = {0, 0}, gk = 0;
+    // Phases continue across items: counters are global to the CTA.  Q load n
+    // of a slot goes to buffer n % NQ.
+    if (warp == kLoadWarp && lane == 0) {
+      uint32_t qn[kSlots] = {0, 0}, gk = 0;
       bool ok = true;
       for (int i = blockIdx.x; ok && i < p.n_items; i += gridDim.x) {
         const Item it = decode_item(p, i, BN);
 #pragma unroll
         for (int t = 0; t < kSlots; ++t) {
           if (!it.nkv[t]) continue;
-          // Q_t is free once the last S MMA of the previous item that read it is done
-          if (qc[t] && !wait(&q_empty[t], (qc[t] - 1) & 1)) { ok = false; break; }
-          unsigned char* sQ = smem + C::OFF_Q + t * C::Q_BYTES;
-          mbar_arrive_expect_tx(&q_full[t], C::Q_BYTES);
+          const uint32_t qb = qn[t] % C::NQ, use = qn[t] / C::NQ;
+          // buffer qb is free once the last S MMA that read it (NQ loads ago) is done
+          if (use && !wait(&q_empty[t * C::NQ + qb], (use - 1) & 1)) { ok = false; break; }
+          unsigned char* sQ = smem + C::OFF_Q + (t * C::NQ + qb) * C::Q_BYTES;
+          mbar_arrive_expect_tx(&q_full[t * C::NQ + qb], C::Q_BYTES);
 #pragma unroll
           for (int db = 0; db < C::DB; ++db)
-            tma_load_4d(sQ + db * BM * 128, &tmQ, db * 64, it.q0[t], it.h[t], it.b, &q_full[t]);
-          ++qc[t];
+            tma_load_4d(sQ + db * BM * 128, &tmQ, db * 64, it.q0[t], it.h[t], it.b, &q_full[t * C::NQ + qb]);
+          ++qn[t];
         }
         for (int j = 0; ok && j < it.L; ++j, ++gk) {
           const uint32_t st = gk % C::NSK;
@@ -375,10 +429,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (*abort_flag) {  // drain loads still in flight into this CTA's shared memory
         for (int t = 0; t < kSlots; ++t)
-          if (qc[t]) mbar_wait(&q_full[t], (qc[t] - 1) & 1);
+          for (uint32_t n = qn[t] > C::NQ ? qn[t] - C::NQ : 0; n < qn[t]; ++n)
+            mbar_wait(&q_full[t * C::NQ + n % C::NQ], (n / C::NQ) & 1);
         for (uint32_t g = gk > C::NSK ? gk - C::NSK : 0; g < gk; ++g) mbar_wait(&k_full[g % C::NSK], (g / C::NSK) & 1);
       }
-    } else if (lane == 1) {
+    } else if (warp == kLoadVWarp && lane == 0) {
       uint32_t gv = 0;
       bool ok = true;
       for (int i = blockIdx.x; ok && i < p.n_items; i += gridDim.x) {
@@ -397,82 +452,78 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (uint32_t g = gv > C::NSV ? gv - C::NSV : 0; g < gv; ++g) mbar_wait(&v_full[g % C::NSV], (g / C::NSV) & 1);
       }
     }
-  } else if (warp == kMmaWarp) {
-    // ========================= MMA issuer =========================
-    // The whole warp runs the loop (descriptors stay warp-uniform); one
-    // elected lane issues each MMA and commit.  Per key tile j: S_0,j and
-    // S_1,j, then P.V of tile j-1 for both slots, so S of the next tile is
-    // ready when a softmax warpgroup finishes the current one.
-    uint32_t gk = 0, gv = 0, qf[kSlots] = {0, 0}, sc[kSlots] = {0, 0}, pc[kSlots] = {0, 0};
+  } else if ((warp == kMmaWarp || warp == kMmaWarp1) && lane == 0) {
+    // ========================= MMA issuers =========================
+    // One thread per slot issues that slot's MMAs and commits, so neither
+    // slot's next S waits behind the other slot's P.V.  Each issuer walks all
+    // key tiles of every item: it waits for each K and V stage and commits
+    // one arrival to its release barrier (count 2) even for tiles its slot
+    // skips.  Per tile: S of tile j, then P.V of tile j-1, so the next S is
+    // queued before the tensor core waits on the softmax, also across items.
+    const int t = warp == kMmaWarp ? 0 : 1;
+    uint32_t gk = 0, gv = 0, qn = 0, sc = 0, pc = 0;
     bool ok = true;
+    bool pend = false, pend_act = false, pend_first = false;  // P.V owed for the previous tile
+    auto issue_pv = [&]() -> bool {
+      const uint32_t st = gv % C::NSV;
+      if (!wait(&v_full[st], (gv / C::NSV) & 1)) return false;
+      if (pend_act) {
+        if (!wait(&p_full[t], pc & 1)) return false;
+        tc_fence_after();
+        const uint32_t sV = smem_u32(smem + C::OFF_V + st * C::KV_BYTES);
+#pragma unroll
+        for (int k = 0; k < BN / 16; ++k)
+          mma_f16_ts(tmem + C::COL_O + t * D, tmem + C::COL_P + t * (BN / 2) + k * 8,
+                     desc_sw128(sV + k * 2048, BN * 128, 1024), IDESC_PV, (!pend_first || k > 0) ? 1u : 0u);
+        mma_commit(&pv_done[t]);
+        ++pc;
+      }
+      mma_commit(&v_empty[st]);
+      ++gv;
+      return true;
+    };
     for (int i = blockIdx.x; ok && i < p.n_items; i += gridDim.x) {
       const Item it = decode_item(p, i, BN);
-      for (int j = 0; ok && j <= it.L; ++j) {
-        if (j < it.L) {
-          const uint32_t st = gk % C::NSK;
-          if (!wwait(&k_full[st], (gk / C::NSK) & 1)) { ok = false; break; }
+      const int nkv = t ? it.nkv[1] : it.nkv[0];
+      for (int j = 0; ok && j < it.L; ++j) {
+        const uint32_t st = gk % C::NSK;
+        if (!wait(&k_full[st], (gk / C::NSK) & 1)) { ok = false; break; }
+        if (j < nkv) {
+          const uint32_t qb = qn % C::NQ, use = qn / C::NQ;
+          if (j == 0 && !wait(&q_full[t * C::NQ + qb], use & 1)) { ok = false; break; }
+          if (sc && !wait(&s_empty[t], (sc - 1) & 1)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t sQ = smem_u32(smem + C::OFF_Q + (t * C::NQ + qb) * C::Q_BYTES);
           const uint32_t sK = smem_u32(smem + C::OFF_K + st * C::KV_BYTES);
 #pragma unroll
-          for (int t = 0; t < kSlots; ++t) {
-            if (j >= it.nkv[t]) continue;
-            if (j == 0 && !wwait(&q_full[t], qf[t]++ & 1)) { ok = false; break; }
-            if (sc[t] && !wwait(&s_empty[t], (sc[t] - 1) & 1)) { ok = false; break; }
-            tc_fence_after();
-            const uint32_t sQ = smem_u32(smem + C::OFF_Q + t * C::Q_BYTES);
-            const bool leader = elect_one();
-#pragma unroll
-            for (int k = 0; k < D / 16; ++k) {
-              const uint32_t offq = (k >> 2) * (BM * 128) + (k & 3) * 32;
-              const uint32_t offk = (k >> 2) * (BN * 128) + (k & 3) * 32;
-              const uint64_t da = desc_sw128(sQ + offq, 16, 1024), db = desc_sw128(sK + offk, 16, 1024);
-              if (leader) mma_f16(tmem + C::COL_S + t * BN, da, db, IDESC_S, k > 0);
-            }
-            if (leader) {
-              mma_commit(&s_full[t]);
-              if (j == it.nkv[t] - 1) mma_commit(&q_empty[t]);
-            }
-            __syncwarp();
-            ++sc[t];
+          for (int k = 0; k < D / 16; ++k) {
+            const uint32_t offq = (k >> 2) * (BM * 128) + (k & 3) * 32;
+            const uint32_t offk = (k >> 2) * (BN * 128) + (k & 3) * 32;
+            mma_f16(tmem + C::COL_S + t * BN, desc_sw128(sQ + offq, 16, 1024), desc_sw128(sK + offk, 16, 1024),
+                    IDESC_S, k > 0);
           }
-          if (!ok) break;
-          if (elect_one()) mma_commit(&k_empty[st]);
-          __syncwarp();
-          ++gk;
-        }
-        if (j >= 1) {
-          const int jj = j - 1;
-          const uint32_t st = gv % C::NSV;
-          if (!wwait(&v_full[st], (gv / C::NSV) & 1)) { ok = false; break; }
-          const uint32_t sV = smem_u32(smem + C::OFF_V + st * C::KV_BYTES);
-#pragma unroll
-          for (int t = 0; t < kSlots; ++t) {
-            if (jj >= it.nkv[t]) continue;
-            if (!wwait(&p_full[t], pc[t] & 1)) { ok = false; break; }
-            tc_fence_after();
-            const bool leader = elect_one();
-#pragma unroll
-            for (int k = 0; k < BN / 16; ++k) {
-              const uint64_t db = desc_sw128(sV + k * 2048, BN * 128, 1024);
-              if (leader)
-                mma_f16_ts(tmem + C::COL_O + t * D, tmem + C::COL_P + t * (BN / 2) + k * 8, db, IDESC_PV,
-                           (jj > 0 || k > 0) ? 1u : 0u);
-            }
-            if (leader) mma_commit(&pv_done[t]);
-            __syncwarp();
-            ++pc[t];
+          mma_commit(&s_full[t]);
+          if (j == nkv - 1) {
+            mma_commit(&q_empty[t * C::NQ + qb]);
+            ++qn;
           }
-          if (!ok) break;
-          if (elect_one()) mma_commit(&v_empty[st]);
-          __syncwarp();
-          ++gv;
+          ++sc;
         }
+        mma_commit(&k_empty[st]);
+        ++gk;
+        if (pend && !issue_pv()) { ok = false; break; }
+        pend = true;
+        pend_first = j == 0;
+        pend_act = j < nkv;
       }
     }
-    // every MMA issued by this warp has finished before the CTA can exit
-    if (elect_one()) mma_commit(mma_idle);
-    __syncwarp();
+    if (ok && pend) issue_pv();
+    // every MMA issued by this thread has finished before the CTA can exit
+    mma_commit(mma_idle);
     mbar_wait(mma_idle, 0);
+  }
   } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kSoftmaxRegs));
     // ========================= softmax warpgroups =========================
     const int t = warp >> 2;                   // slot
     const int r = threadIdx.x & (BM - 1);      // row in the tile = TMEM lane
@@ -480,8 +531,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t tS = tmem + lane_addr + C::COL_S + t * BN;
     const uint32_t tO = tmem + lane_addr + C::COL_O + t * D;
     const uint32_t tP = tmem + lane_addr + C::COL_P + t * (BN / 2);
-    uint32_t sc = 0, pc = 0;
-    bool ok = true;
+    uint32_t sc = 0, pc = 0, pn = 0;           // S tiles read, P.V completions seen, P tiles written
+    // The output of an item is written after the first tile of the next one
+    // has been exponentiated, so the wait for the item's last P.V is hidden.
+    T* pend_orow = nullptr;
+    float pend_inv = 0.f;
+    bool ok = true, pend_out = false;
     for (int i = blockIdx.x; ok && i < p.n_items; i += gridDim.x) {
       const Item it = decode_item(p, i, BN);
       // slot fields selected without dynamic indexing (keeps Item in registers)
@@ -570,20 +625,23 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float2 rsum = __fadd2_rn(rs01, rs23);
         l = l * alpha + (rsum.x + rsum.y);
         // P_t and O_t are free once the previous P.V of this slot is done
-        if (j >= 1) {
+        if (pn) {
           if (!wait(&pv_done[t], pc & 1)) { ok = false; break; }
           ++pc;
           tc_fence_after();
-          if (__any_sync(0xffffffffu, need)) {
+        }
+        if (j == 0) {
+          if (pend_out) write_output<T, D>(tO, pend_orow, pend_inv);  // previous item, O final
+          pend_out = false;
+        } else if (__any_sync(0xffffffffu, need)) {
 #pragma unroll
-            for (int c = 0; c < D / 32; ++c) {
-              uint32_t rr[32];
-              tmem_ld32(tO + c * 32, rr);
-              tmem_wait_ld();
+          for (int c = 0; c < D / 32; ++c) {
+            uint32_t rr[32];
+            tmem_ld32(tO + c * 32, rr);
+            tmem_wait_ld();
 #pragma unroll
-              for (int e = 0; e < 32; ++e) rr[e] = __float_as_uint(__uint_as_float(rr[e]) * alpha);
-              tmem_st32(tO + c * 32, rr);
-            }
+            for (int e = 0; e < 32; ++e) rr[e] = __float_as_uint(__uint_as_float(rr[e]) * alpha);
+            tmem_st32(tO + c * 32, rr);
           }
         }
 #pragma unroll
@@ -592,38 +650,24 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&p_full[t]);
+        ++pn;
       }
       if (!ok) break;
-      // ---- epilogue: O / l for valid rows, zeros for var-len padding rows
-      if (!wait(&pv_done[t], pc & 1)) { ok = false; break; }
+      // O / l for valid rows, zeros for var-len padding rows; rows past S not stored
+      pend_out = true;
+      pend_orow = row < p.S ? orow : nullptr;
+      pend_inv = (l > 0.f && row < it.seq_len) ? 1.f / l : 0.f;
+    }
+    if (ok && pend_out && wait(&pv_done[t], pc & 1)) {
       ++pc;
       tc_fence_after();
-      const float inv = (l > 0.f && row < it.seq_len) ? 1.f / l : 0.f;
-#pragma unroll
-      for (int c = 0; c < D / 32; ++c) {
-        uint32_t rr[32];
-        tmem_ld32(tO + c * 32, rr);
-        tmem_wait_ld();
-        if (row < p.S) {
-#pragma unroll
-          for (int e = 0; e < 32; e += 8) {
-            uint4 w;
-            w.x = Elem<T>::pack2(__uint_as_float(rr[e + 0]) * inv, __uint_as_float(rr[e + 1]) * inv);
-            w.y = Elem<T>::pack2(__uint_as_float(rr[e + 2]) * inv, __uint_as_float(rr[e + 3]) * inv);
-            w.z = Elem<T>::pack2(__uint_as_float(rr[e + 4]) * inv, __uint_as_float(rr[e + 5]) * inv);
-            w.w = Elem<T>::pack2(__uint_as_float(rr[e + 6]) * inv, __uint_as_float(rr[e + 7]) * inv);
-            *reinterpret_cast<uint4*>(orow + c * 32 + e) = w;
-          }
-        }
-      }
-      // O_t is overwritten by the next item's first P.V only after this
-      // warpgroup's p_full arrive, which follows these loads in program order
-      tc_fence_before();
+      write_output<T, D>(tO, pend_orow, pend_inv);
     }
   }
   tc_fence_before();
   __syncthreads();
   if (warp == kMmaWarp) {
+    __syncwarp();
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(C::TMEM_COLS));
   }
@@ -678,6 +722,15 @@ int launch_prefill(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorM
                    cudaStream_t st) {
   auto kern = prefill_fwd_kernel<T, D>;
   const int smem = (int)Cfg<D>::SMEM;
+  // the register split in the kernel is only valid at the compiled count
+  static int regs = -1;
+  if (regs < 0) {
+    cudaFuncAttributes fa;
+    regs = cudaFuncGetAttributes(&fa, kern) == cudaSuccess ? fa.numRegs : 0;
+  }
+  if (regs != kLaunchRegs)
+    return set_error(AKT_ERR_CUDA, "prefill kernel compiled with " + std::to_string(regs) + " registers, expected " +
+                                       std::to_string(kLaunchRegs));
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return set_error(AKT_ERR_CUDA, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
   const int grid = std::min(p.n_items, sm_count());  // persistent: one CTA per SM
@@ -693,6 +746,14 @@ int launch_prefill(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorM
 bool al16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; }
 
 }  // namespace
+
+cudaError_t prefill_status_read(unsigned int* v) { return cudaMemcpyFromSymbol(v, g_device_status_local, sizeof(*v)); }
+
+cudaError_t prefill_status_clear() {
+  const unsigned int z = 0;
+  return cudaMemcpyToSymbol(g_device_status_local, &z, sizeof(z));
+}
+
 }  // namespace akt
 
 using namespace akt;
