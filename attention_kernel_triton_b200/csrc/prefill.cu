@@ -30,10 +30,9 @@
 //
 // The running max used for exponentiation only moves when the row max grows
 // by more than 8 (log2 units), so O is rescaled rarely (P <= 2^8 stays exact
-// enough in fp16/bf16 relative terms; the final O/l is unchanged).  On key
-// tiles without masking a share of the exponentials is evaluated on the FMA
-// pipe by a polynomial (exp2_poly2) instead of the MUFU unit, whose 16
-// results per clock per SM would otherwise bound a head_dim-64 kernel.
+// enough in fp16/bf16 relative terms; the final O/l is unchanged).  At
+// head_dim 64 the exponentials bound the kernel: MUFU ex2 delivers 16
+// results per clock per SM, 256 flops of the two MMAs per result.
 // Built without -rdc (whole-program device code): with relocatable device
 // code ptxas ignores setmaxnreg, and the softmax warpgroups need its budget.
 #define AKT_WHOLE_PROGRAM 1
@@ -71,12 +70,6 @@ constexpr int kControlRegs = 64;
 static_assert(2 * 128 * kSoftmaxRegs + 128 * kControlRegs <= kThreads * kLaunchRegs, "register split");
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 
-// 8-element chunks of a row evaluated by the FMA-pipe polynomial (of BN/8) on
-// key tiles without masking; the rest use MUFU ex2.
-#ifndef AKT_PREFILL_POLY_CHUNKS
-#define AKT_PREFILL_POLY_CHUNKS 0
-#endif
-
 // Tile configuration per head_dim D.  Keys per tile BN is chosen so that
 // S[2], O[2] and P[2] fit the 512 TMEM columns of one SM:
 //   D=64 : BN=128 -> 256 + 128 + 128 = 512 columns; smem 64 KB Q + 3-stage K, V rings = 160 KB
@@ -92,8 +85,6 @@ struct Cfg {
   static_assert(COL_P + BN <= TMEM_COLS, "TMEM budget");
   static constexpr int NQ = 2;                            // Q buffers per slot (next item's Q loads early)
   static constexpr int NSK = D == 64 ? 3 : 2, NSV = NSK;  // K / V ring stages
-  static constexpr int CHUNKS = BN / 8;
-  static constexpr int POLY = AKT_PREFILL_POLY_CHUNKS < CHUNKS ? AKT_PREFILL_POLY_CHUNKS : CHUNKS;
   static constexpr uint32_t Q_BYTES = BM * D * 2;         // one slot
   static constexpr uint32_t KV_BYTES = BN * D * 2;        // one K or V tile
   static constexpr uint32_t OFF_Q = 0;
@@ -246,29 +237,6 @@ __device__ __forceinline__ float max3f(float a, float b, float c) {
   float r;
   asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
   return r;
-}
-
-// 2^x on the FMA/ALU pipes for a pair of values, x <= ~8 (larger arguments are
-// not produced: the running max trails the row max by at most 8).  x is
-// clamped to -126 (2^-126 rounds to zero in fp16/bf16), split as x = j + f with
-// j = round-to-nearest(x) read from the low mantissa bits of x + 1.5*2^23 and
-// f in [-0.5, 0.5]; 2^f = 1 + f(c1 + f(c2 + f c3)), a degree-3 fit with the
-// constant term fixed at 1 and the other coefficients minimising the maximum
-// relative error on [-0.5, 0.5] (1.0e-4, below half an fp16 ulp); 2^j is added
-// to the exponent field.
-__device__ __forceinline__ float2 exp2_poly2(float2 x) {
-  constexpr float kShift = 12582912.0f;  // 1.5 * 2^23
-  constexpr float c1 = 0.693282961845398f, c2 = 0.2422109991312027f, c3 = 0.055008918046951294f;
-  x.x = fmaxf(x.x, -126.f);
-  x.y = fmaxf(x.y, -126.f);
-  const float2 t = __fadd2_rn(x, make_float2(kShift, kShift));
-  const float2 j = __fadd2_rn(t, make_float2(-kShift, -kShift));
-  const float2 f = __ffma2_rn(j, make_float2(-1.f, -1.f), x);
-  float2 q = __ffma2_rn(make_float2(c3, c3), f, make_float2(c2, c2));
-  q = __ffma2_rn(q, f, make_float2(c1, c1));
-  q = __ffma2_rn(q, f, make_float2(1.f, 1.f));
-  return make_float2(__uint_as_float(__float_as_uint(q.x) + (__float_as_uint(t.x) << 23)),
-                     __uint_as_float(__float_as_uint(q.y) + (__float_as_uint(t.y) << 23)));
 }
 
 template <typename T>
@@ -604,22 +572,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int e = 0; e < 4; ++e) rs2[e] = make_float2(0.f, 0.f);
         uint32_t pk[BN / 64][32];
-        if (masked || C::POLY == 0) {
 #pragma unroll
-          for (int e = 0; e < BN / 2; ++e) {
-            const float2 v = ffma2(make_float2(x[2 * e], x[2 * e + 1]), sl2, nm2);
-            const float2 ev = make_float2(fast_exp2(v.x), fast_exp2(v.y));
-            rs2[e & 3] = __fadd2_rn(rs2[e & 3], ev);
-            pk[e >> 5][e & 31] = pack_p<T>(ev.x, ev.y);
-          }
-        } else {
-#pragma unroll
-          for (int e = 0; e < BN / 2; ++e) {
-            const float2 v = ffma2(make_float2(x[2 * e], x[2 * e + 1]), sl2, nm2);
-            const float2 ev = (e / 4) < C::POLY ? exp2_poly2(v) : make_float2(fast_exp2(v.x), fast_exp2(v.y));
-            rs2[e & 3] = __fadd2_rn(rs2[e & 3], ev);
-            pk[e >> 5][e & 31] = pack_p<T>(ev.x, ev.y);
-          }
+        for (int e = 0; e < BN / 2; ++e) {
+          const float2 v = ffma2(make_float2(x[2 * e], x[2 * e + 1]), sl2, nm2);
+          const float2 ev = make_float2(fast_exp2(v.x), fast_exp2(v.y));
+          rs2[e & 3] = __fadd2_rn(rs2[e & 3], ev);
+          pk[e >> 5][e & 31] = pack_p<T>(ev.x, ev.y);
         }
         const float2 rs01 = __fadd2_rn(rs2[0], rs2[1]), rs23 = __fadd2_rn(rs2[2], rs2[3]);
         const float2 rsum = __fadd2_rn(rs01, rs23);
