@@ -24,7 +24,8 @@ AKT_FLOAT16 = 0
 AKT_BFLOAT16 = 1
 
 DEVICE_STATUS_NAMES = {0: "ok", 1: "wait timeout", 2: "page id outside the pool",
-                       3: "token index outside the sequence", 4: "malformed indptr"}
+                       3: "token index outside the sequence", 4: "malformed indptr",
+                       5: "kept-index list longer than its buffer"}
 
 
 class AktError(RuntimeError):
@@ -112,6 +113,25 @@ class PrefillArgs(Structure):
     ]
 
 
+class MaskToIndexArgs(Structure):
+    _fields_ = [
+        ("mask", c_void_p), ("mask_stride_batch", c_int64), ("mask_stride_head", c_int64),
+        ("sparse_ind", c_void_p), ("ind_stride_batch", c_int64), ("ind_stride_head", c_int64),
+        ("sparse_nnz", c_void_p), ("nnz_stride_batch", c_int64), ("nnz_stride_head", c_int64),
+        ("batch", c_int32), ("num_heads", c_int32), ("seq_len", c_int32), ("max_kept", c_int32),
+        ("keep_first_if_empty", c_int32),
+    ]
+
+
+class IndexToMaskArgs(Structure):
+    _fields_ = [
+        ("sparse_ind", c_void_p), ("ind_stride_batch", c_int64), ("ind_stride_head", c_int64),
+        ("sparse_nnz", c_void_p), ("nnz_stride_batch", c_int64), ("nnz_stride_head", c_int64),
+        ("mask", c_void_p), ("mask_stride_batch", c_int64), ("mask_stride_head", c_int64),
+        ("batch", c_int32), ("num_heads", c_int32), ("seq_len", c_int32), ("max_kept", c_int32),
+    ]
+
+
 # name -> (restype, argtypes); every function declared in include/akt.h
 SIGNATURES = {
     "akt_abi_version": (c_int, []),
@@ -138,6 +158,8 @@ SIGNATURES = {
                                            c_void_p]),
     "akt_lse_merge": (c_int, [c_void_p, c_int64, c_void_p, c_int64, c_int32, c_int64, c_int32, c_void_p, c_int64,
                               c_int32, c_void_p]),
+    "akt_mask_to_sparse_index": (c_int, [POINTER(MaskToIndexArgs), c_void_p]),
+    "akt_sparse_index_to_mask": (c_int, [POINTER(IndexToMaskArgs), c_void_p]),
 }
 
 _lib = None

@@ -34,6 +34,7 @@ enum DeviceStatus : unsigned int {
   kStatusBadPage = 2,         // page id outside the pool
   kStatusBadToken = 3,        // token index outside the sequence
   kStatusBadIndptr = 4,       // indptr not monotone / past the index array
+  kStatusListOverflow = 5,    // more kept tokens than the index list holds
 };
 
 __device__ __forceinline__ void record_status(unsigned int code) {

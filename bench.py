@@ -234,6 +234,16 @@ def secondary_measurements(dev, iters=20, only=None):
                                                                      sd.softmax_scale, sd.group), iters, dev, flush)
         return {"gbs": sd.bytes / ms / 1e6, "ms": ms, "mb": sd.bytes / 1e6, "l2": "flushed"}
 
+    def mask_to_index(L, L_max):
+        def run():
+            from attention_kernel_triton_b200.sparse_index import sparse_index_from_mask
+            g = torch.Generator(device=dev).manual_seed(43)
+            mask = torch.rand((1, 32, L), generator=g, device=dev) < 0.02
+            ms = time_kernels(lambda: sparse_index_from_mask(mask, L_max), iters, dev, flush)
+            nbytes = mask.numel() + 32 * L_max * 4 + 32 * 4  # mask read, lists and nnz written
+            return {"gbs": nbytes / ms / 1e6, "ms": ms, "mb": nbytes / 1e6, "l2": "flushed"}
+        return run
+
     table = [
         ("prefill_cfg0_causal", prefill_cfg0),
         ("prefill_cfg1_varlen", prefill_cfg1),
@@ -245,6 +255,8 @@ def secondary_measurements(dev, iters=20, only=None):
         ("sparse_cfg4_paged", sparse_paged(False)),
         ("magicpig_cfg4_paged", sparse_paged(True)),
         ("sparse_128k_single_sequence", sparse_128k),
+        ("mask_to_index_cfg4", mask_to_index(32000, 3840)),
+        ("mask_to_index_128k", mask_to_index(131072, 4096)),
     ]
     out = {}
     for name, fn in table:

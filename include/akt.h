@@ -46,7 +46,8 @@ int akt_abi_version(void);
 const char* akt_last_error(void);
 /* First error code any kernel recorded on `device` since the last clear
  * (0 = none; 1 wait timeout, 2 page id out of pool, 3 token index out of
- * sequence, 4 malformed indptr).  Synchronises that device. */
+ * sequence, 4 malformed indptr, 5 kept-index list longer than its buffer).
+ * Synchronises that device. */
 int akt_device_status(int device, unsigned int* status_out);
 int akt_clear_device_status(int device);
 
@@ -257,6 +258,46 @@ int akt_magicpig_paged_partial(const akt_sparse_paged_args* args, float* o_part,
 int akt_lse_merge(const float* o_parts, int64_t o_part_stride, const float* lse_parts, int64_t lse_part_stride,
                   int32_t num_parts, int64_t rows, int32_t head_dim, void* out, int64_t out_row_stride,
                   int32_t dtype, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* keep mask <-> padded kept-index lists, on the device                     */
+/* replaces the Python loops of                                             */
+/* sparsetoken_decode_flash_attention_redundant.py:283-295 (a per-token     */
+/* keep mask to sparse_ind / sparse_nnz) and :317-324 (the lists back to    */
+/* precompute_mask); the reference has no library function for either.     */
+/* mask -> lists: kept positions ascending, the rest of each list -1; an    */
+/* empty mask keeps token 0 when keep_first_if_empty (the reference's       */
+/* rule); more than max_kept kept tokens keeps the first max_kept and       */
+/* records status 5.  lists -> mask: nnz 0 reads as 1, entries are Python   */
+/* indices (negative counts from the end, so -1 padding marks the last      */
+/* token, as the reference loop does); entries outside [-seq_len, seq_len)  */
+/* are skipped and recorded (status 3).  Masks are bytes (torch.bool), one  */
+/* per token, token stride 1; lists have position stride 1.                 */
+/* ------------------------------------------------------------------------ */
+typedef struct akt_mask_to_index_args {
+  const uint8_t* mask; /* [batch, num_heads, seq_len] */
+  int64_t mask_stride_batch, mask_stride_head;
+  int32_t* sparse_ind; /* [batch, num_heads, max_kept] (output) */
+  int64_t ind_stride_batch, ind_stride_head;
+  int32_t* sparse_nnz; /* [batch, num_heads(, 1)] (output) */
+  int64_t nnz_stride_batch, nnz_stride_head;
+  int32_t batch, num_heads, seq_len, max_kept;
+  int32_t keep_first_if_empty;
+} akt_mask_to_index_args;
+
+int akt_mask_to_sparse_index(const akt_mask_to_index_args* args, void* stream);
+
+typedef struct akt_index_to_mask_args {
+  const int32_t* sparse_ind; /* [batch, num_heads, max_kept] */
+  int64_t ind_stride_batch, ind_stride_head;
+  const int32_t* sparse_nnz; /* [batch, num_heads(, 1)] */
+  int64_t nnz_stride_batch, nnz_stride_head;
+  uint8_t* mask; /* [batch, num_heads, seq_len] (output) */
+  int64_t mask_stride_batch, mask_stride_head;
+  int32_t batch, num_heads, seq_len, max_kept;
+} akt_index_to_mask_args;
+
+int akt_sparse_index_to_mask(const akt_index_to_mask_args* args, void* stream);
 
 #ifdef __cplusplus
 }

@@ -190,6 +190,25 @@ def sparsetoken_naive_decode_by_mask(q, K, V, sparse_ind, sparse_nnz, softmax_sc
     return torch.matmul(torch.softmax(s, dim=-1), V)
 
 
+def sparse_lists_from_mask(kept_mask, L_max: int):
+    """Kept-index lists from a per-row keep mask, as the reference's driver builds
+    them (SD:283-295): ascending positions, the rest -1, an empty row keeps token 0.
+    Returns ``(sparse_ind [B,H,L_max] int32, sparse_nnz [B,H,1] int32)``."""
+    m = _c(kept_mask, torch.bool).clone()
+    B, H, _ = m.shape
+    ind = torch.full((B, H, L_max), -1, dtype=torch.int32)
+    nnz = torch.zeros((B, H, 1), dtype=torch.int32)
+    for b in range(B):
+        for h in range(H):
+            n = int(m[b, h].sum())
+            if n == 0:
+                n = 1
+                m[b, h, 0] = True
+            nnz[b, h, 0] = n
+            ind[b, h, :n] = torch.nonzero(m[b, h], as_tuple=False).squeeze(-1)
+    return ind, nnz
+
+
 def sparse_mask_from_lists(sparse_ind, sparse_nnz, seq_len: int) -> torch.Tensor:
     """The keep mask the reference's driver builds from the lists (SD:315-324)."""
     ind = _c(sparse_ind, torch.int64)

@@ -49,6 +49,39 @@ def nested_function(path: str, outer: str, inner: str, env: dict):
     raise KeyError(f"{outer}.{inner} not found in {path}")
 
 
+def loop_in(path: str, outer: str, target: str, must_contain: str) -> str:
+    """Source of the top-level-in-body ``for <target> in ...`` loop of function ``outer``
+    whose text contains ``must_contain`` (dedented to column 0)."""
+    src = open(path).read()
+    for node in ast.parse(src).body:
+        if isinstance(node, ast.FunctionDef) and node.name == outer:
+            for sub in ast.walk(node):
+                if isinstance(sub, ast.For) and ast.unparse(sub.target) == target:
+                    seg = ast.get_source_segment(src, sub)
+                    if must_contain in seg:
+                        pad = " " * sub.col_offset
+                        return "\n".join(l[len(pad):] if l.startswith(pad) else l for l in seg.splitlines())
+    raise KeyError(f"{outer}: for {target} ... {must_contain}")
+
+
+class _SeededTorch(types.ModuleType):
+    """``torch`` for an exec'd reference loop: ``torch.rand`` draws from a seeded
+    CPU generator and records every draw; everything else is torch."""
+
+    def __init__(self, seed: int):
+        super().__init__("torch")
+        self._g = torch.Generator().manual_seed(seed)
+        self.draws = []
+
+    def rand(self, size, device=None, **kw):
+        r = torch.rand(size, generator=self._g)
+        self.draws.append(r)
+        return r
+
+    def __getattr__(self, name):
+        return getattr(torch, name)
+
+
 def f32(t):
     return t.float()
 
@@ -166,6 +199,28 @@ def main():
                                                       c.sparse_ind, c.sparse_nnz, c.K, c.L)
     save("magicpig_paged", q=c.q, cache=c.cache, indptr=c.indptr, indices=c.indices,
          sparse_ind=c.sparse_ind, sparse_nnz=c.sparse_nnz, K=c.K, L=c.L, O=O)
+
+
+    # ---------------- keep mask <-> kept-index lists (SD:283-295 and SD:317-324), the
+    # reference's own loops run on seeded draws; the raw keep mask is recovered from them
+    sd_path = os.path.join(ref, "sparsetoken_decode_flash_attention_redundant.py")
+    gen_loop = loop_in(sd_path, "test_op_decode_sparsetoken", "bh", "sparse_ind")
+    mask_loop = loop_in(sd_path, "test_op_decode_sparsetoken", "b", "precompute_mask")
+    B, H, SEQ_LEN, kept_ratio = 2, 6, 300, 0.006  # a few rows draw nothing and keep token 0
+    L_max = int(SEQ_LEN * (kept_ratio + 0.1))
+    shim = _SeededTorch(701)
+    env = {"torch": shim, "BATCH_SIZE": B, "num_qo_heads": H, "kept_ratio": kept_ratio, "device": "cpu",
+           "original_nzz": torch.full((B, H, 1), SEQ_LEN, dtype=torch.int32),
+           "sparse_ind": torch.zeros((B, H, L_max), dtype=torch.int32) - 1}
+    exec(compile(gen_loop, f"{sd_path}:mask->lists", "exec"), env)
+    kept_mask = torch.stack([d < kept_ratio for d in shim.draws]).reshape(B, H, SEQ_LEN)
+    sparse_ind, sparse_nnz = env["sparse_ind"], env["original_nzz"]
+    env2 = {"torch": torch, "BATCH_SIZE": B, "num_qo_heads": H, "sparse_nnz": sparse_nnz,
+            "sparse_ind": sparse_ind,
+            "precompute_mask": torch.zeros((B, H, SEQ_LEN), dtype=torch.bool)}
+    exec(compile(mask_loop, f"{sd_path}:lists->mask", "exec"), env2)
+    save("mask_index", kept_mask=kept_mask, L_max=L_max, sparse_ind=sparse_ind, sparse_nnz=sparse_nnz,
+         precompute_mask=env2["precompute_mask"])
 
 
 if __name__ == "__main__":

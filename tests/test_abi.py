@@ -50,6 +50,8 @@ STRUCTS = {
     "akt_decode_paged_args": _lib.DecodePagedArgs,
     "akt_sparse_dense_args": _lib.SparseDenseArgs,
     "akt_sparse_paged_args": _lib.SparsePagedArgs,
+    "akt_mask_to_index_args": _lib.MaskToIndexArgs,
+    "akt_index_to_mask_args": _lib.IndexToMaskArgs,
 }
 
 

@@ -111,3 +111,14 @@ def test_lse_merge_reference_is_exact_split():
     ls.append(torch.full((3,), float("-inf"), dtype=torch.float64))
     merged = N.lse_merge_reference(torch.stack(os_), torch.stack(ls))
     assert maxabs(merged, full) <= 1e-12
+
+
+def test_mask_index_oracles_match_reference_loops():
+    f = load("mask_index")
+    ind, nnz = N.sparse_lists_from_mask(f["kept_mask"], int(f["L_max"]))
+    assert torch.equal(ind, f["sparse_ind"]) and torch.equal(nnz, f["sparse_nnz"])
+    m = N.sparse_mask_from_lists(f["sparse_ind"], f["sparse_nnz"], f["kept_mask"].shape[2])
+    assert torch.equal(m, f["precompute_mask"])
+    # an empty row's list is [0, -1, ...]; reading it back marks token 0 only
+    empty = f["kept_mask"].sum(-1) == 0
+    assert empty.any() and torch.all(f["precompute_mask"][empty].sum(-1) == 1)
