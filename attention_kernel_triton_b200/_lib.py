@@ -158,6 +158,10 @@ SIGNATURES = {
                                            c_void_p]),
     "akt_lse_merge": (c_int, [c_void_p, c_int64, c_void_p, c_int64, c_int32, c_int64, c_int32, c_void_p, c_int64,
                               c_int32, c_void_p]),
+    "akt_sparse_dense_csr": (c_int, [POINTER(SparseDenseArgs), c_void_p, c_int64, c_void_p, c_size_t, c_void_p]),
+    "akt_sparse_paged_csr": (c_int, [POINTER(SparsePagedArgs), c_void_p, c_int64, c_void_p, c_size_t, c_void_p]),
+    "akt_magicpig_paged_csr": (c_int, [POINTER(SparsePagedArgs), c_void_p, c_int64, c_void_p, c_size_t,
+                                       c_void_p]),
     "akt_mask_to_sparse_index": (c_int, [POINTER(MaskToIndexArgs), c_void_p]),
     "akt_sparse_index_to_mask": (c_int, [POINTER(IndexToMaskArgs), c_void_p]),
 }

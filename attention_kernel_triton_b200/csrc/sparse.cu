@@ -53,6 +53,10 @@ struct SparseParams {
   int64_t ind_sb, ind_sh, ind_sp;
   const int32_t* nnz;
   int64_t nnz_sb, nnz_sh;
+  // CSR lists (instead of ind/nnz): row r = b * Hq + h holds
+  // ind[csr_ptr[r] .. csr_ptr[r + 1]) of a flat index array of num_inds entries
+  const int32_t* csr_ptr;
+  int64_t num_inds;
   const float* mp_k;
   const float* mp_l;
   int64_t par_sb, par_sh;
@@ -76,7 +80,18 @@ struct SparseParams {
 // planner: chunks per (batch, unit) = ceil(max nnz over the unit's heads / kCP)
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ int clamped_nnz(const SparseParams& p, int b, int h) {
-  int n = p.nnz[(int64_t)b * p.nnz_sb + (int64_t)h * p.nnz_sh];
+  int n;
+  if (p.csr_ptr) {
+    const int64_t r = (int64_t)b * p.Hq + h;
+    const int s = __ldg(p.csr_ptr + r), e = __ldg(p.csr_ptr + r + 1);
+    if (s < 0 || e < s || e > p.num_inds) {  // malformed row offsets: the row keeps nothing
+      record_status(kStatusBadIndptr);
+      return 0;
+    }
+    n = e - s;
+  } else {
+    n = p.nnz[(int64_t)b * p.nnz_sb + (int64_t)h * p.nnz_sh];
+  }
   if (n > p.max_nnz) {
     record_status(kStatusBadToken);
     n = p.max_nnz;
@@ -318,9 +333,12 @@ __global__ void __launch_bounds__(kSThreads) sparse_decode_kernel(const SparsePa
     for (int e = cta.tid; e < G * kCP; e += kSThreads) {
       const int h = e / kCP, j = e - h * kCP;
       const int pos = p0 + j;
-      cta.idx_s[e] = pos < cta.nnz_s[h]
-                         ? p.ind[(int64_t)b * p.ind_sb + (int64_t)(head0 + h) * p.ind_sh + (int64_t)pos * p.ind_sp]
-                         : -1;
+      if (pos >= cta.nnz_s[h])
+        cta.idx_s[e] = -1;
+      else if (p.csr_ptr)  // row offset checked by clamped_nnz (nnz 0 if malformed)
+        cta.idx_s[e] = p.ind[(int64_t)__ldg(p.csr_ptr + (int64_t)b * p.Hq + head0 + h) + pos];
+      else
+        cta.idx_s[e] = p.ind[(int64_t)b * p.ind_sb + (int64_t)(head0 + h) * p.ind_sh + (int64_t)pos * p.ind_sp];
     }
     __syncthreads();
     bool same = true;
@@ -480,7 +498,8 @@ void fill_common(SparseParams& p, const SparsePlan& pl, void* ws) {
 }
 
 int paged_entry(const akt_sparse_paged_args* a, void* ws, size_t ws_bytes, void* stream, bool magic,
-                float* o_part = nullptr, float* lse_part = nullptr) {
+                float* o_part = nullptr, float* lse_part = nullptr, const int32_t* csr_ptr = nullptr,
+                int64_t num_inds = 0) {
   if (!a) return set_error(AKT_ERR_INVALID, "null args");
   int rc = check_heads(a->batch, a->num_qo_heads, a->num_kv_heads, a->head_dim, a->dtype, a->max_nnz);
   if (rc) return rc;
@@ -503,6 +522,7 @@ int paged_entry(const akt_sparse_paged_args* a, void* ws, size_t ws_bytes, void*
   p.num_pages = a->num_pages; p.num_page_entries = a->num_page_entries;
   p.ind = a->sparse_ind; p.ind_sb = a->ind_stride_batch; p.ind_sh = a->ind_stride_head; p.ind_sp = a->ind_stride_pos;
   p.nnz = a->sparse_nnz; p.nnz_sb = a->nnz_stride_batch; p.nnz_sh = a->nnz_stride_head;
+  p.csr_ptr = csr_ptr; p.num_inds = num_inds;
   p.mp_k = a->magicpig_k; p.mp_l = a->magicpig_l; p.par_sb = a->param_stride_batch; p.par_sh = a->param_stride_head;
   p.out = a->out; p.o_sb = a->out_stride_batch; p.o_sh = a->out_stride_head; p.o_sd = a->out_stride_dim;
   p.B = a->batch; p.Hq = a->num_qo_heads; p.Hkv = a->num_kv_heads; p.L = 0; p.P = a->page_size;
@@ -534,7 +554,8 @@ size_t akt_sparse_dense_workspace_size(const akt_sparse_dense_args* a) {
 }
 
 static int sparse_dense_entry(const akt_sparse_dense_args* a, void* ws, size_t ws_bytes, void* stream,
-                              float* o_part, float* lse_part) {
+                              float* o_part, float* lse_part, const int32_t* csr_ptr = nullptr,
+                              int64_t num_inds = 0) {
   if (!a) return set_error(AKT_ERR_INVALID, "null args");
   int rc = check_heads(a->batch, a->num_qo_heads, a->num_kv_heads, a->head_dim, a->dtype, a->max_nnz);
   if (rc) return rc;
@@ -556,6 +577,7 @@ static int sparse_dense_entry(const akt_sparse_dense_args* a, void* ws, size_t w
   p.s0 = a->k_stride_batch; p.s_head = a->k_stride_head; p.s_tok = a->k_stride_token;
   p.ind = a->sparse_ind; p.ind_sb = a->ind_stride_batch; p.ind_sh = a->ind_stride_head; p.ind_sp = a->ind_stride_pos;
   p.nnz = a->sparse_nnz; p.nnz_sb = a->nnz_stride_batch; p.nnz_sh = a->nnz_stride_head;
+  p.csr_ptr = csr_ptr; p.num_inds = num_inds;
   p.out = a->out; p.o_sb = a->out_stride_batch; p.o_sh = a->out_stride_head; p.o_sd = a->out_stride_dim;
   p.B = a->batch; p.Hq = a->num_qo_heads; p.Hkv = a->num_kv_heads; p.L = a->seq_len; p.P = 1;
   p.max_nnz = a->max_nnz;
@@ -571,6 +593,24 @@ static int sparse_dense_entry(const akt_sparse_dense_args* a, void* ws, size_t w
 
 int akt_sparse_dense(const akt_sparse_dense_args* a, void* ws, size_t ws_bytes, void* stream) {
   return sparse_dense_entry(a, ws, ws_bytes, stream, nullptr, nullptr);
+}
+
+int akt_sparse_dense_csr(const akt_sparse_dense_args* a, const int32_t* sparse_ptr, int64_t num_inds, void* ws,
+                         size_t ws_bytes, void* stream) {
+  if (!sparse_ptr || num_inds < 0) return set_error(AKT_ERR_INVALID, "CSR lists need sparse_ptr and num_inds >= 0");
+  return sparse_dense_entry(a, ws, ws_bytes, stream, nullptr, nullptr, sparse_ptr, num_inds);
+}
+
+int akt_sparse_paged_csr(const akt_sparse_paged_args* a, const int32_t* sparse_ptr, int64_t num_inds, void* ws,
+                         size_t ws_bytes, void* stream) {
+  if (!sparse_ptr || num_inds < 0) return set_error(AKT_ERR_INVALID, "CSR lists need sparse_ptr and num_inds >= 0");
+  return paged_entry(a, ws, ws_bytes, stream, false, nullptr, nullptr, sparse_ptr, num_inds);
+}
+
+int akt_magicpig_paged_csr(const akt_sparse_paged_args* a, const int32_t* sparse_ptr, int64_t num_inds, void* ws,
+                           size_t ws_bytes, void* stream) {
+  if (!sparse_ptr || num_inds < 0) return set_error(AKT_ERR_INVALID, "CSR lists need sparse_ptr and num_inds >= 0");
+  return paged_entry(a, ws, ws_bytes, stream, true, nullptr, nullptr, sparse_ptr, num_inds);
 }
 
 int akt_sparse_dense_partial(const akt_sparse_dense_args* a, float* o_part, float* lse_part, void* ws,

@@ -16,7 +16,7 @@ import math
 
 import torch
 
-from .sparsetoken_decode_flash_attention_redundant_var_len_paged import sparse_paged_call
+from .sparsetoken_decode_flash_attention_redundant_var_len_paged import csr_max_nnz, sparse_paged_call
 
 
 def magicpig_sparsetoken_flash_attention_decode_paged(q, paged_kv_cache, kv_page_indptr, kv_page_indices, sparse_ind,
@@ -25,3 +25,18 @@ def magicpig_sparsetoken_flash_attention_decode_paged(q, paged_kv_cache, kv_page
     output = torch.empty((B, H_q, D), device=q.device, dtype=q.dtype)
     return sparse_paged_call("akt_magicpig_paged", output, q, paged_kv_cache, kv_page_indptr, kv_page_indices,
                              sparse_ind, sparse_nnz, 1.0 / math.sqrt(D), K=K, L=L)
+
+
+def magicpig_sparsetoken_flash_attention_decode_paged_csr(q, paged_kv_cache, kv_page_indptr, kv_page_indices,
+                                                          sparse_inds, sparse_ptr, K, L, max_nnz=None):
+    """CSR-list variant: head ``h`` of batch ``b`` keeps
+    ``sparse_inds[sparse_ptr[b*Hq + h] : sparse_ptr[b*Hq + h + 1]]`` (the ``inds`` + ``ptr``
+    format of ``sparse_decode_flash_attention.py:13-15``).  -> O [B, Hq, D]."""
+    B, H_q, _, D = q.shape
+    assert sparse_ptr.numel() == B * H_q + 1, "sparse_ptr must hold B * Hq + 1 offsets"
+    if max_nnz is None:
+        max_nnz = csr_max_nnz(sparse_ptr)
+    output = torch.empty((B, H_q, D), device=q.device, dtype=q.dtype)
+    return sparse_paged_call("akt_magicpig_paged_csr", output, q, paged_kv_cache, kv_page_indptr, kv_page_indices,
+                             sparse_inds.reshape(-1), None, 1.0 / math.sqrt(D), K=K, L=L,
+                             csr=(sparse_ptr.reshape(-1), max_nnz))

@@ -13,6 +13,9 @@ current stream, with the reference's rules:
   ``-1``; an empty row keeps token 0 (``nnz = 1``).  A row with more than
   ``L_max`` kept tokens keeps the first ``L_max`` and records device status 5
   (the reference's slice assignment raises there).
+* :func:`sparse_csr_from_lists` -- the padded lists as CSR (``inds`` + ``ptr``,
+  the format the reference's notes propose, ``sparse_decode_flash_attention.py:13-15``),
+  for the ``*_csr`` decode entry points.
 * :func:`precompute_mask` -- ``nnz == 0`` reads as 1 and entries are Python
   indices, so a negative entry counts from the end (the ``-1`` padding of an
   empty list marks the last token, exactly as the reference loop does);
@@ -75,3 +78,18 @@ def precompute_mask(sparse_ind: torch.Tensor, sparse_nnz: torch.Tensor, SEQ_LEN:
     a.batch, a.num_heads, a.seq_len, a.max_kept = B, H, SEQ_LEN, L_max
     _lib.check(_lib.lib().akt_sparse_index_to_mask(ctypes.byref(a), _lib.stream_ptr(dev)))
     return mask
+
+
+def sparse_csr_from_lists(sparse_ind: torch.Tensor, sparse_nnz: torch.Tensor):
+    """Padded lists ``(sparse_ind [B, H, L_max], sparse_nnz [B, H(, 1)])`` -> CSR
+    ``(inds [sum nnz] int32, ptr [B*H + 1] int32)``: row ``b*H + h`` is
+    ``inds[ptr[b*H + h] : ptr[b*H + h + 1]]``, the first ``nnz`` entries of that list
+    (``nnz`` clamped to ``[0, L_max]``).  Device-side torch ops, no host copy."""
+    dev = _lib.require_cuda(sparse_ind, sparse_nnz)
+    B, H, L_max = sparse_ind.shape
+    n = sparse_nnz.reshape(B * H).to(torch.int64).clamp(0, L_max)
+    ptr = torch.zeros(B * H + 1, dtype=torch.int64, device=dev)
+    ptr[1:] = torch.cumsum(n, 0)
+    keep = torch.arange(L_max, device=dev).unsqueeze(0) < n.unsqueeze(1)
+    inds = sparse_ind.reshape(B * H, L_max)[keep].to(torch.int32)
+    return inds, ptr.to(torch.int32)

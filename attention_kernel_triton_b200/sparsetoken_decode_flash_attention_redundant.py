@@ -19,8 +19,10 @@ from . import _lib
 redundant_len = 16  # reference module constant (SD:7)
 
 
-def _sparse_dense_call(entry, out, q, K, V, sparse_ind, sparse_nnz, softmax_scale, GQA_group_size, partial=None):
-    """Shared launcher; ``partial=(o_part, lse_part)`` selects the partial-output entry point."""
+def _sparse_dense_call(entry, out, q, K, V, sparse_ind, sparse_nnz, softmax_scale, GQA_group_size, partial=None,
+                       csr=None):
+    """Shared launcher; ``partial=(o_part, lse_part)`` selects the partial-output entry point,
+    ``csr=(sparse_ptr, max_nnz)`` the CSR-list one (``sparse_ind`` is then the flat index array)."""
     dev = _lib.require_cuda(q, K, V)
     if not (q.dtype == K.dtype == V.dtype) or (out is not None and out.dtype != q.dtype):
         raise TypeError("q, K, V and the output must share one dtype")
@@ -29,7 +31,8 @@ def _sparse_dense_call(entry, out, q, K, V, sparse_ind, sparse_nnz, softmax_scal
     assert Hq % Hkv == 0
     assert Hq // Hkv == GQA_group_size
     ind = _lib.as_int32(sparse_ind, dev)
-    nnz = _lib.as_int32(sparse_nnz, dev)
+    nnz = _lib.as_int32(sparse_nnz, dev) if csr is None else None
+    ptr = _lib.as_int32(csr[0], dev) if csr is not None else None
     t = {"q": q, "K": K, "V": V}
     L = _lib.lib()
     fn = getattr(L, entry)
@@ -43,20 +46,25 @@ def _sparse_dense_call(entry, out, q, K, V, sparse_ind, sparse_nnz, softmax_scal
         a.k_stride_batch, a.k_stride_head, a.k_stride_token, a.k_stride_dim = KK.stride()
         a.v = VV.data_ptr()
         a.v_stride_batch, a.v_stride_head, a.v_stride_token, a.v_stride_dim = VV.stride()
-        (a.ind_stride_batch, a.ind_stride_head, a.ind_stride_pos), (a.nnz_stride_batch, a.nnz_stride_head) = \
-            _lib.index_strides(ind, nnz)
-        a.sparse_ind, a.sparse_nnz = ind.data_ptr(), nnz.data_ptr()
+        if csr is None:
+            (a.ind_stride_batch, a.ind_stride_head, a.ind_stride_pos), (a.nnz_stride_batch, a.nnz_stride_head) = \
+                _lib.index_strides(ind, nnz)
+            a.sparse_ind, a.sparse_nnz = ind.data_ptr(), nnz.data_ptr()
+            a.max_nnz = ind.shape[2]
+        else:
+            a.sparse_ind, a.max_nnz = ind.data_ptr(), int(csr[1])
         if out is not None:
             a.out = out.data_ptr()
             a.out_stride_batch, a.out_stride_head, a.out_stride_dim = out.stride(0), out.stride(1), out.stride(3)
         a.batch, a.num_qo_heads, a.num_kv_heads, a.seq_len, a.head_dim = B, Hq, Hkv, KK.shape[2], D
-        a.max_nnz = ind.shape[2]
         a.dtype = _lib.dtype_code(qq)
         a.softmax_scale = float(softmax_scale)
         ws = _lib.workspace(L.akt_sparse_dense_workspace_size(ctypes.byref(a)), dev)
         if partial is not None:
             return fn(ctypes.byref(a), partial[0].data_ptr(), partial[1].data_ptr(), ws.data_ptr(), ws.numel(),
                       _lib.stream_ptr(dev))
+        if csr is not None:
+            return fn(ctypes.byref(a), ptr.data_ptr(), ind.numel(), ws.data_ptr(), ws.numel(), _lib.stream_ptr(dev))
         return fn(ctypes.byref(a), ws.data_ptr(), ws.numel(), _lib.stream_ptr(dev))
 
     def contiguous():
@@ -88,3 +96,21 @@ def sparsetoken_flash_attention_decode(q, K, V, sparse_ind, sparse_nnz, softmax_
     B, Hq, _, D = q.shape
     O = torch.empty((B, Hq, 1, D), dtype=q.dtype, device=q.device)
     return sparse_dense_into(O, q, K, V, sparse_ind, sparse_nnz, softmax_scale, GQA_group_size)
+
+
+def sparsetoken_flash_attention_decode_csr(q, K, V, sparse_inds, sparse_ptr, softmax_scale, GQA_group_size,
+                                           max_nnz=None):
+    """CSR-list variant (the ``inds`` + ``ptr`` format of the reference's notes,
+    ``sparse_decode_flash_attention.py:13-15``): head ``h`` of batch ``b`` keeps
+    ``sparse_inds[sparse_ptr[b*Hq + h] : sparse_ptr[b*Hq + h + 1]]`` (ascending token positions).
+    ``max_nnz`` bounds the row lengths (it sizes the split-KV scratch); when omitted it is
+    read from ``sparse_ptr`` with one device-to-host copy.  -> O [B, Hq, 1, D]."""
+    B, Hq, _, D = q.shape
+    if max_nnz is None:
+        max_nnz = int((sparse_ptr[1:] - sparse_ptr[:-1]).max().item()) if sparse_ptr.numel() > 1 else 0
+    O = torch.empty((B, Hq, 1, D), dtype=q.dtype, device=q.device)
+    _lib.require_cuda(O, sparse_inds, sparse_ptr)
+    assert sparse_ptr.numel() == B * Hq + 1, "sparse_ptr must hold B * Hq + 1 offsets"
+    _sparse_dense_call("akt_sparse_dense_csr", O, q, K, V, sparse_inds.reshape(-1), None, softmax_scale,
+                       GQA_group_size, csr=(sparse_ptr.reshape(-1), max_nnz))
+    return O

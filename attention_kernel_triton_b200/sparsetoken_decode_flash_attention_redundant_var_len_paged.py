@@ -21,7 +21,9 @@ redundant_len = 16  # reference module constant (SP:7)
 
 
 def sparse_paged_call(entry, out, q, paged_kv_cache, kv_page_indptr, kv_page_indices, sparse_ind, sparse_nnz,
-                      softmax_scale, K=None, L=None):
+                      softmax_scale, K=None, L=None, csr=None):
+    """Shared launcher; ``csr=(sparse_ptr, max_nnz)`` selects a CSR-list entry point
+    (``sparse_ind`` is then the flat index array and ``sparse_nnz`` is not used)."""
     dev = _lib.require_cuda(q, paged_kv_cache, out)
     if not (q.dtype == paged_kv_cache.dtype == out.dtype):
         raise TypeError("q, paged_kv_cache and the output must share one dtype")
@@ -31,14 +33,15 @@ def sparse_paged_call(entry, out, q, paged_kv_cache, kv_page_indptr, kv_page_ind
     indptr = _lib.as_int32(kv_page_indptr, dev)
     indices = _lib.as_int32(kv_page_indices, dev)
     ind = _lib.as_int32(sparse_ind, dev)
-    nnz = _lib.as_int32(sparse_nnz, dev)
+    nnz = _lib.as_int32(sparse_nnz, dev) if csr is None else None
+    ptr = _lib.as_int32(csr[0], dev) if csr is not None else None
     t = {"q": q, "cache": paged_kv_cache}
     if K is not None:
         t["K"] = K.to(device=dev, dtype=torch.float32)
         t["L"] = L.to(device=dev, dtype=torch.float32)
     lib = _lib.lib()
     fn = getattr(lib, entry)
-    wsfn = getattr(lib, entry + "_workspace_size")
+    wsfn = getattr(lib, entry.replace("_csr", "") + "_workspace_size")
 
     def call():
         a = _lib.SparsePagedArgs()
@@ -49,9 +52,12 @@ def sparse_paged_call(entry, out, q, paged_kv_cache, kv_page_indptr, kv_page_ind
         (a.kv_stride_page, a.kv_stride_kv, a.kv_stride_head, a.kv_stride_token, a.kv_stride_dim) = cache.stride()
         a.num_pages = cache.shape[0]
         a.kv_page_indptr, a.kv_page_indices, a.num_page_entries = indptr.data_ptr(), indices.data_ptr(), indices.numel()
-        (a.ind_stride_batch, a.ind_stride_head, a.ind_stride_pos), (a.nnz_stride_batch, a.nnz_stride_head) = \
-            _lib.index_strides(ind, nnz)
-        a.sparse_ind, a.sparse_nnz = ind.data_ptr(), nnz.data_ptr()
+        if csr is None:
+            (a.ind_stride_batch, a.ind_stride_head, a.ind_stride_pos), (a.nnz_stride_batch, a.nnz_stride_head) = \
+                _lib.index_strides(ind, nnz)
+            a.sparse_ind, a.sparse_nnz = ind.data_ptr(), nnz.data_ptr()
+        else:
+            a.sparse_ind = ind.data_ptr()
         if "K" in t:
             a.magicpig_k, a.magicpig_l = t["K"].data_ptr(), t["L"].data_ptr()
             if t["K"].shape != (B, Hq) or t["K"].stride() != t["L"].stride():
@@ -61,10 +67,13 @@ def sparse_paged_call(entry, out, q, paged_kv_cache, kv_page_indptr, kv_page_ind
         a.out = out.data_ptr()
         a.out_stride_batch, a.out_stride_head, a.out_stride_dim = out.stride()
         a.batch, a.num_qo_heads, a.num_kv_heads = B, Hq, cache.shape[2]
-        a.page_size, a.head_dim, a.max_nnz = cache.shape[3], D, ind.shape[2]
+        a.page_size, a.head_dim = cache.shape[3], D
+        a.max_nnz = ind.shape[2] if csr is None else int(csr[1])
         a.dtype = _lib.dtype_code(qq)
         a.softmax_scale = float(softmax_scale)
         ws = _lib.workspace(wsfn(ctypes.byref(a)), dev)
+        if csr is not None:
+            return fn(ctypes.byref(a), ptr.data_ptr(), ind.numel(), ws.data_ptr(), ws.numel(), _lib.stream_ptr(dev))
         return fn(ctypes.byref(a), ws.data_ptr(), ws.numel(), _lib.stream_ptr(dev))
 
     def contiguous():
@@ -83,3 +92,24 @@ def sparsetoken_flash_attention_decode_paged(q, paged_kv_cache, kv_page_indptr, 
     O = torch.empty((B, Hq, D), dtype=q.dtype, device=q.device)
     return sparse_paged_call("akt_sparse_paged", O, q, paged_kv_cache, kv_page_indptr, kv_page_indices, sparse_ind,
                              sparse_nnz, 1.0 / math.sqrt(D))
+
+
+def csr_max_nnz(sparse_ptr):
+    """Longest CSR row (one device-to-host copy)."""
+    return int((sparse_ptr[1:] - sparse_ptr[:-1]).max().item()) if sparse_ptr.numel() > 1 else 0
+
+
+def sparsetoken_flash_attention_decode_paged_csr(q, paged_kv_cache, kv_page_indptr, kv_page_indices, sparse_inds,
+                                                 sparse_ptr, max_nnz=None):
+    """CSR-list variant (``inds`` + ``ptr``, the format of the reference's notes,
+    ``sparse_decode_flash_attention.py:13-15``): head ``h`` of batch ``b`` keeps
+    ``sparse_inds[sparse_ptr[b*Hq + h] : sparse_ptr[b*Hq + h + 1]]``.  ``max_nnz`` bounds the
+    row lengths (read from ``sparse_ptr`` when omitted).  -> O [B, Hq, D]."""
+    B, Hq, _, D = q.shape
+    assert sparse_ptr.numel() == B * Hq + 1, "sparse_ptr must hold B * Hq + 1 offsets"
+    if max_nnz is None:
+        max_nnz = csr_max_nnz(sparse_ptr)
+    O = torch.empty((B, Hq, D), dtype=q.dtype, device=q.device)
+    return sparse_paged_call("akt_sparse_paged_csr", O, q, paged_kv_cache, kv_page_indptr, kv_page_indices,
+                             sparse_inds.reshape(-1), None, 1.0 / math.sqrt(D),
+                             csr=(sparse_ptr.reshape(-1), max_nnz))

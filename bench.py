@@ -179,7 +179,7 @@ def secondary_measurements(dev, iters=20, only=None):
     from attention_kernel_triton_b200.prefill_flash_attention_var_len_padding import (
         flash_attention_prefill as flash_attention_prefill_varlen)
     from attention_kernel_triton_b200.sparsetoken_decode_flash_attention_redundant import (
-        sparsetoken_flash_attention_decode)
+        sparsetoken_flash_attention_decode, sparsetoken_flash_attention_decode_csr)
     from attention_kernel_triton_b200.sparsetoken_decode_flash_attention_redundant_var_len_paged import (
         sparsetoken_flash_attention_decode_paged)
     hbm, _ = measured_peaks()
@@ -234,6 +234,17 @@ def secondary_measurements(dev, iters=20, only=None):
                                                                      sd.softmax_scale, sd.group), iters, dev, flush)
         return {"gbs": sd.bytes / ms / 1e6, "ms": ms, "mb": sd.bytes / 1e6, "l2": "flushed"}
 
+    def sparse_128k_csr():
+        from attention_kernel_triton_b200.sparse_index import sparse_csr_from_lists
+        sd = W.make_sparse_dense(B=1, Hq=32, Hkv=8, L=131072, D=128, keep_p=0.02, seed=12, device=dev, L_max=4096)
+        inds, ptr = sparse_csr_from_lists(sd.sparse_ind, sd.sparse_nnz)
+        ms = time_kernels(lambda: sparsetoken_flash_attention_decode_csr(sd.q, sd.K, sd.V, inds, ptr,
+                                                                         sd.softmax_scale, sd.group, max_nnz=4096),
+                          iters, dev, flush)
+        return {"gbs": sd.bytes / ms / 1e6, "ms": ms, "mb": sd.bytes / 1e6, "l2": "flushed",
+                "index_bytes_csr": (inds.numel() + ptr.numel()) * 4,
+                "index_bytes_padded": sd.sparse_ind.numel() * 4 + sd.sparse_nnz.numel() * 4}
+
     def mask_to_index(L, L_max):
         def run():
             from attention_kernel_triton_b200.sparse_index import sparse_index_from_mask
@@ -255,6 +266,7 @@ def secondary_measurements(dev, iters=20, only=None):
         ("sparse_cfg4_paged", sparse_paged(False)),
         ("magicpig_cfg4_paged", sparse_paged(True)),
         ("sparse_128k_single_sequence", sparse_128k),
+        ("sparse_128k_csr", sparse_128k_csr),
         ("mask_to_index_cfg4", mask_to_index(32000, 3840)),
         ("mask_to_index_128k", mask_to_index(131072, 4096)),
     ]

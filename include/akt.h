@@ -236,6 +236,27 @@ size_t akt_magicpig_paged_workspace_size(const akt_sparse_paged_args* args);
 int akt_magicpig_paged(const akt_sparse_paged_args* args, void* workspace, size_t workspace_bytes, void* stream);
 
 /* ------------------------------------------------------------------------ */
+/* sparse-token decodes with CSR kept-index lists                           */
+/* The "inds + ptr" index format proposed in the reference's notes          */
+/* (sparse_decode_flash_attention.py:13-15), which has no implementation    */
+/* there: the kept tokens of (batch b, qo head h) are                       */
+/* args->sparse_ind[sparse_ptr[r] .. sparse_ptr[r + 1]) with                */
+/* r = b * num_qo_heads + h, so lists are not padded to a common length.    */
+/* sparse_ptr holds batch * num_qo_heads + 1 offsets into a flat array of   */
+/* num_inds entries; args->sparse_nnz and the ind strides are not read;     */
+/* args->max_nnz bounds every row's length (it sizes the workspace, as      */
+/* *_workspace_size reports for the same args; longer rows are cut there   */
+/* and recorded, status 3).  Rows with malformed offsets keep nothing and   */
+/* are recorded (status 4).  Same kernels and semantics otherwise.          */
+/* ------------------------------------------------------------------------ */
+int akt_sparse_dense_csr(const akt_sparse_dense_args* args, const int32_t* sparse_ptr, int64_t num_inds,
+                         void* workspace, size_t workspace_bytes, void* stream);
+int akt_sparse_paged_csr(const akt_sparse_paged_args* args, const int32_t* sparse_ptr, int64_t num_inds,
+                         void* workspace, size_t workspace_bytes, void* stream);
+int akt_magicpig_paged_csr(const akt_sparse_paged_args* args, const int32_t* sparse_ptr, int64_t num_inds,
+                           void* workspace, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------ */
 /* KV split across devices (long single-sequence sparse decode)             */
 /* No reference counterpart (the reference keeps no LSE; its store is       */
 /* commented out at prefill_flash_attention.py:331-334).  The *_partial     */

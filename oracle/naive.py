@@ -209,6 +209,21 @@ def sparse_lists_from_mask(kept_mask, L_max: int):
     return ind, nnz
 
 
+def sparse_lists_from_csr(inds, ptr, B: int, H: int):
+    """CSR kept-index rows (``inds`` + ``ptr``, the format of SS:13-15; row ``b*H + h`` is
+    ``inds[ptr[r]:ptr[r+1]]``) as the padded ``(sparse_ind, sparse_nnz)`` the naive
+    references take; the padding length is the longest row (at least 1)."""
+    inds, ptr = _c(inds, torch.int64), _c(ptr, torch.int64)
+    n = (ptr[1:] - ptr[:-1]).reshape(B, H)
+    L_max = max(int(n.max()) if n.numel() else 0, 1)
+    ind = torch.full((B, H, L_max), -1, dtype=torch.int32)
+    for b in range(B):
+        for h in range(H):
+            r = b * H + h
+            ind[b, h, : int(n[b, h])] = inds[int(ptr[r]):int(ptr[r + 1])].to(torch.int32)
+    return ind, n.to(torch.int32).unsqueeze(-1)
+
+
 def sparse_mask_from_lists(sparse_ind, sparse_nnz, seq_len: int) -> torch.Tensor:
     """The keep mask the reference's driver builds from the lists (SD:315-324)."""
     ind = _c(sparse_ind, torch.int64)
