@@ -132,6 +132,20 @@ class IndexToMaskArgs(Structure):
     ]
 
 
+class AppendPagedArgs(Structure):
+    _fields_ = [
+        ("kv_cache", c_void_p), ("kv_stride_page", c_int64), ("kv_stride_kv", c_int64), ("kv_stride_head", c_int64),
+        ("kv_stride_token", c_int64), ("kv_stride_dim", c_int64), ("num_pages", c_int64),
+        ("kv_page_indptr", c_void_p), ("kv_page_indices", c_void_p), ("kv_last_page_len", c_void_p),
+        ("num_page_entries", c_int64),
+        ("append_k", c_void_p), ("k_stride_token", c_int64), ("k_stride_head", c_int64), ("k_stride_dim", c_int64),
+        ("append_v", c_void_p), ("v_stride_token", c_int64), ("v_stride_head", c_int64), ("v_stride_dim", c_int64),
+        ("append_indptr", c_void_p), ("num_append", c_int64),
+        ("batch", c_int32), ("num_kv_heads", c_int32), ("page_size", c_int32), ("head_dim", c_int32),
+        ("dtype", c_int32),
+    ]
+
+
 # name -> (restype, argtypes); every function declared in include/akt.h
 SIGNATURES = {
     "akt_abi_version": (c_int, []),
@@ -141,6 +155,7 @@ SIGNATURES = {
     "akt_profile_enable": (c_int, [c_int]),
     "akt_profile_read": (c_int, [POINTER(ctypes.c_double), POINTER(c_int64)]),
     "akt_prefill": (c_int, [POINTER(PrefillArgs), c_void_p]),
+    "akt_prefill_with_lse": (c_int, [POINTER(PrefillArgs), c_void_p, c_int64, c_int64, c_void_p]),
     "akt_decode_dense_workspace_size": (c_size_t, [POINTER(DecodeDenseArgs)]),
     "akt_decode_dense": (c_int, [POINTER(DecodeDenseArgs), c_void_p, c_size_t, c_void_p]),
     "akt_decode_paged_workspace_size": (c_size_t, [POINTER(DecodePagedArgs)]),
@@ -162,6 +177,7 @@ SIGNATURES = {
     "akt_sparse_paged_csr": (c_int, [POINTER(SparsePagedArgs), c_void_p, c_int64, c_void_p, c_size_t, c_void_p]),
     "akt_magicpig_paged_csr": (c_int, [POINTER(SparsePagedArgs), c_void_p, c_int64, c_void_p, c_size_t,
                                        c_void_p]),
+    "akt_append_paged_kv": (c_int, [POINTER(AppendPagedArgs), c_void_p]),
     "akt_mask_to_sparse_index": (c_int, [POINTER(MaskToIndexArgs), c_void_p]),
     "akt_sparse_index_to_mask": (c_int, [POINTER(IndexToMaskArgs), c_void_p]),
 }

@@ -9,9 +9,15 @@ import torch
 from . import _lib
 
 
-def prefill_into(O, Q, K, V, causal, softmax_scale, GQA_group_size, varlen=None):
-    """Write ``softmax(Q K^T * scale [causal]) V`` (GQA) into ``O [B, H, S, D]``."""
+def prefill_into(O, Q, K, V, causal, softmax_scale, GQA_group_size, varlen=None, lse=None):
+    """Write ``softmax(Q K^T * scale [causal]) V`` (GQA) into ``O [B, H, S, D]``; with
+    ``lse`` (fp32 ``[B, H, S]``, token stride 1) also each row's natural-log sum-exp of the
+    scaled scores over its visible keys (-inf for var-len padding rows)."""
     dev = _lib.require_cuda(Q, K, V, O)
+    if lse is not None:
+        _lib.require_cuda(lse)
+        if lse.dtype != torch.float32 or lse.shape != O.shape[:3] or lse.stride(2) != 1:
+            raise ValueError("lse must be fp32 [B, H, S] with token stride 1")
     if not (Q.dtype == K.dtype == V.dtype == O.dtype):
         raise TypeError("Q, K, V and the output must share one dtype")
     B, H, S, D = Q.shape
@@ -39,6 +45,9 @@ def prefill_into(O, Q, K, V, causal, softmax_scale, GQA_group_size, varlen=None)
         a.causal = 1 if causal else 0
         a.dtype = _lib.dtype_code(qq)
         a.softmax_scale = float(softmax_scale)
+        if lse is not None:
+            return L.akt_prefill_with_lse(ctypes.byref(a), lse.data_ptr(), lse.stride(0), lse.stride(1),
+                                          _lib.stream_ptr(dev))
         return L.akt_prefill(ctypes.byref(a), _lib.stream_ptr(dev))
 
     def contiguous():

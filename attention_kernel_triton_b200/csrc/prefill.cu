@@ -63,10 +63,10 @@ constexpr int kLoadVWarp = 10;     // the V ring (its own warp: two waiting lane
 constexpr int kMmaWarp1 = 11;      // MMA issuer of slot 1 (slot 0: kMmaWarp)
 // Register split: the kernel is compiled for 168 registers per thread (3 warps
 // per SM sub-partition); the producer/MMA warpgroup gives registers back and
-// the softmax warpgroups take them: 2*128*216 + 128*64 <= 384*168.
+// the softmax warpgroups take them: 2*128*224 + 128*56 <= 384*168.
 constexpr int kLaunchRegs = 168;
-constexpr int kSoftmaxRegs = 216;
-constexpr int kControlRegs = 64;
+constexpr int kSoftmaxRegs = 224;
+constexpr int kControlRegs = 56;
 static_assert(2 * 128 * kSoftmaxRegs + 128 * kControlRegs <= kThreads * kLaunchRegs, "register split");
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 
@@ -110,6 +110,8 @@ struct PrefillParams {
   int pair_heads;            // 1: slots are qo heads 2p, 2p+1 at the same rows; 0: query tiles 2p, 2p+1 of one head
   int causal;
   float scale_log2;
+  float* lse;                // [B, Hq, S] natural-log sum-exp per row, or null
+  int64_t lse_sb, lse_sh;
 };
 
 // One work item: the key-tile count of each slot (0 = slot has no valid rows).
@@ -515,6 +517,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (row < p.S) {
 #pragma unroll
           for (int c = 0; c < D; c += 8) *reinterpret_cast<uint4*>(orow + c) = make_uint4(0, 0, 0, 0);
+          if (p.lse) p.lse[(int64_t)it.b * p.lse_sb + (int64_t)hq * p.lse_sh + row] = -INFINITY;
         }
         continue;
       }
@@ -614,7 +617,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       // O / l for valid rows, zeros for var-len padding rows; rows past S not stored
       pend_out = true;
       pend_orow = row < p.S ? orow : nullptr;
-      pend_inv = (l > 0.f && row < it.seq_len) ? 1.f / l : 0.f;
+      const bool has_keys = l > 0.f && row < it.seq_len;
+      pend_inv = has_keys ? 1.f / l : 0.f;
+      // LSE in natural log (final once the last tile is exponentiated): the
+      // running max is kept in log2 units and P = 2^(x - m)
+      if (p.lse && row < p.S)
+        p.lse[(int64_t)it.b * p.lse_sb + (int64_t)hq * p.lse_sh + row] =
+            has_keys ? (m_use + __log2f(l)) * kLn2 : -INFINITY;
     }
     if (ok && pend_out && wait(&pv_done[t], pc & 1)) {
       ++pc;
@@ -716,7 +725,7 @@ cudaError_t prefill_status_clear() {
 
 using namespace akt;
 
-extern "C" int akt_prefill(const akt_prefill_args* a, void* stream) {
+static int prefill_entry(const akt_prefill_args* a, float* lse, int64_t lse_sb, int64_t lse_sh, void* stream) {
   if (!a) return set_error(AKT_ERR_INVALID, "null args");
   if (a->batch < 0 || a->num_qo_heads <= 0 || a->num_kv_heads <= 0 || a->seq_len < 0)
     return set_error(AKT_ERR_INVALID, "sizes must be non-negative");
@@ -758,9 +767,20 @@ extern "C" int akt_prefill(const akt_prefill_args* a, void* stream) {
   p.n_items = (int)items;
   p.causal = a->causal ? 1 : 0;
   p.scale_log2 = a->softmax_scale * kLog2e;
+  p.lse = lse;
+  p.lse_sb = lse_sb;
+  p.lse_sh = lse_sh;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (a->dtype == AKT_FLOAT16)
     return a->head_dim == 64 ? launch_prefill<__half, 64>(mq, mk, mv, p, st) : launch_prefill<__half, 128>(mq, mk, mv, p, st);
   return a->head_dim == 64 ? launch_prefill<__nv_bfloat16, 64>(mq, mk, mv, p, st)
                            : launch_prefill<__nv_bfloat16, 128>(mq, mk, mv, p, st);
+}
+
+extern "C" int akt_prefill(const akt_prefill_args* a, void* stream) { return prefill_entry(a, nullptr, 0, 0, stream); }
+
+extern "C" int akt_prefill_with_lse(const akt_prefill_args* a, float* lse, int64_t lse_stride_batch,
+                                    int64_t lse_stride_head, void* stream) {
+  if (!lse) return set_error(AKT_ERR_INVALID, "prefill: lse output required");
+  return prefill_entry(a, lse, lse_stride_batch, lse_stride_head, stream);
 }

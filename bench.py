@@ -245,6 +245,20 @@ def secondary_measurements(dev, iters=20, only=None):
                 "index_bytes_csr": (inds.numel() + ptr.numel()) * 4,
                 "index_bytes_padded": sd.sparse_ind.numel() * 4 + sd.sparse_nnz.numel() * 4}
 
+    def append_cfg0():
+        # write path ahead of paged decode: cfg0's K/V (8 x 1024 tokens, 16 kv heads, D=64) into a P=16 pool
+        from attention_kernel_triton_b200.paged_kv_append import append_paged_kv_cache
+        c = W.make_paged(B=8, Hq=64, Hkv=16, D=64, page_size=16, lens=[1024] * 8, seed=44, device=dev)
+        g = torch.Generator(device=dev).manual_seed(44)
+        k = torch.randn((8 * 1024, 16, 64), generator=g, device=dev, dtype=torch.float16)
+        v = torch.randn((8 * 1024, 16, 64), generator=g, device=dev, dtype=torch.float16)
+        app = torch.arange(0, 8 * 1024 + 1, 1024, dtype=torch.int32, device=dev)
+        ms = time_kernels(lambda: append_paged_kv_cache(c.cache, k, v, app, c.indptr, c.indices, c.last_page_len),
+                          iters, dev, flush)
+        nbytes = 2 * 2 * k.numel() * 2  # K and V rows read and written
+        return {"gbs": nbytes / ms / 1e6, "ms": ms, "frac_of_hbm": nbytes / ms / 1e6 / hbm, "mb": nbytes / 1e6,
+                "l2": "flushed"}
+
     def mask_to_index(L, L_max):
         def run():
             from attention_kernel_triton_b200.sparse_index import sparse_index_from_mask
@@ -267,6 +281,7 @@ def secondary_measurements(dev, iters=20, only=None):
         ("magicpig_cfg4_paged", sparse_paged(True)),
         ("sparse_128k_single_sequence", sparse_128k),
         ("sparse_128k_csr", sparse_128k_csr),
+        ("append_paged_cfg0_kv", append_cfg0),
         ("mask_to_index_cfg4", mask_to_index(32000, 3840)),
         ("mask_to_index_128k", mask_to_index(131072, 4096)),
     ]

@@ -89,6 +89,14 @@ typedef struct akt_prefill_args {
 
 int akt_prefill(const akt_prefill_args* args, void* stream);
 
+/* akt_prefill that also writes each row's natural-log sum-exp of the scaled   */
+/* scores over its visible keys, lse [batch, num_qo_heads, seq_len] fp32      */
+/* (token stride 1; -inf for var-len padding rows).  The reference computes  */
+/* this value and leaves its store commented out                             */
+/* (prefill_flash_attention.py:331-334: tmp_m_i += tl.math.log(tmp_l_i)).    */
+int akt_prefill_with_lse(const akt_prefill_args* args, float* lse, int64_t lse_stride_batch,
+                         int64_t lse_stride_head, void* stream);
+
 /* ------------------------------------------------------------------------ */
 /* dense ("redundant") GQA decode                                           */
 /* replaces flash_attention_decode(q, K, V, softmax_scale, GQA_group_size)  */
@@ -279,6 +287,38 @@ int akt_magicpig_paged_partial(const akt_sparse_paged_args* args, float* o_part,
 int akt_lse_merge(const float* o_parts, int64_t o_part_stride, const float* lse_parts, int64_t lse_part_stride,
                   int32_t num_parts, int64_t rows, int32_t head_dim, void* out, int64_t out_row_stride,
                   int32_t dtype, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* paged KV cache append (write path; no reference counterpart: the         */
+/* reference builds its pools in Python, decode_flash_attention_redundant_  */
+/* var_len_paged.py:337-353)                                                 */
+/* The page table (same CSR format as the paged decodes) already covers the */
+/* appended tokens: sequence b holds len_b = (pages_b - 1) * page_size +    */
+/* kv_last_page_len[b] tokens after the append, the last n_b =              */
+/* append_indptr[b+1] - append_indptr[b] of them new.  Appended row i of    */
+/* sequence b (row append_indptr[b] + i of append_k / append_v, each        */
+/* [num_append, num_kv_heads, head_dim]) is written at position             */
+/* len_b - n_b + i.  Bad page ids / positions / indptrs are skipped and     */
+/* recorded (status 2 / 3 / 4).  No workspace.                              */
+/* ------------------------------------------------------------------------ */
+typedef struct akt_append_paged_args {
+  void* kv_cache; /* [num_pages, 2, num_kv_heads, page_size, head_dim] */
+  int64_t kv_stride_page, kv_stride_kv, kv_stride_head, kv_stride_token, kv_stride_dim;
+  int64_t num_pages;
+  const int32_t* kv_page_indptr;   /* [batch + 1] */
+  const int32_t* kv_page_indices;  /* [num_page_entries] */
+  const int32_t* kv_last_page_len; /* [batch], after the append */
+  int64_t num_page_entries;
+  const void* append_k; /* [num_append, num_kv_heads, head_dim] */
+  int64_t k_stride_token, k_stride_head, k_stride_dim;
+  const void* append_v;
+  int64_t v_stride_token, v_stride_head, v_stride_dim;
+  const int32_t* append_indptr; /* [batch + 1] */
+  int64_t num_append;
+  int32_t batch, num_kv_heads, page_size, head_dim, dtype;
+} akt_append_paged_args;
+
+int akt_append_paged_kv(const akt_append_paged_args* args, void* stream);
 
 /* ------------------------------------------------------------------------ */
 /* keep mask <-> padded kept-index lists, on the device                     */

@@ -75,6 +75,24 @@ def prefill_reference(Q, K, V, causal: bool, softmax_scale: float, GQA_group_siz
     return torch.matmul(P, V)
 
 
+def prefill_lse_reference(Q, K, V, causal: bool, softmax_scale: float, GQA_group_size: int = 1, varlen=None,
+                          dtype=F32) -> torch.Tensor:
+    """Per-row log-sum-exp of the scaled scores over the visible keys, the value the
+    reference computes at PF:331 (``tmp_m_i += log(tmp_l_i)``) and does not store.
+    Var-len padding rows (``i >= varlen[b]``) are -inf."""
+    Q, K = _c(Q, dtype), _c(K, dtype)
+    K = K.repeat_interleave(GQA_group_size, dim=1)
+    S = Q.shape[2]
+    s = torch.matmul(Q, K.transpose(-2, -1)) * softmax_scale
+    if causal:
+        s = s.masked_fill(~torch.tril(torch.ones(S, S, dtype=torch.bool)), float("-inf"))
+    lse = torch.logsumexp(s, dim=-1)
+    if varlen is not None:
+        for b, n in enumerate(_c(torch.as_tensor(varlen), torch.int64).tolist()):
+            lse[b, :, int(n):] = float("-inf")
+    return lse
+
+
 def prefill_varlen_reference(Q, K, V, causal: bool, softmax_scale: float, GQA_group_size: int,
                              varlen, dtype=F32, p_round=None) -> torch.Tensor:
     """PV:428-438 followed by the test's zeroing of padded rows (PV:447-450).
@@ -151,6 +169,30 @@ def naive_paged_attention(q, paged_kv_cache, kv_page_indptr, kv_page_indices, kv
         w = torch.softmax(scores, dim=-1)
         out[b] = torch.matmul(w, vseq).squeeze(1)
     return out
+
+
+def append_paged_kv_reference(paged_kv_cache, append_k, append_v, append_indptr, kv_page_indptr, kv_page_indices,
+                              kv_last_page_len):
+    """Write appended rows into a copy of the pool, one token at a time: sequence b holds
+    ``(pages_b - 1) * P + last_b`` tokens after the append, the last ``n_b`` of them new;
+    new row ``i`` goes to position ``len_b - n_b + i`` (page ``indices[indptr[b] + pos // P]``,
+    row ``pos % P``), the addressing of the paged decode (DP:170-174)."""
+    cache = paged_kv_cache.detach().cpu().clone()
+    k, v = append_k.detach().cpu(), append_v.detach().cpu()
+    ip = _c(kv_page_indptr, torch.int64).tolist()
+    ind = _c(kv_page_indices, torch.int64).tolist()
+    last = _c(kv_last_page_len, torch.int64).tolist()
+    ap = _c(append_indptr, torch.int64).tolist()
+    P = cache.shape[3]
+    for b in range(len(ip) - 1):
+        n = ap[b + 1] - ap[b]
+        length = (ip[b + 1] - ip[b] - 1) * P + last[b]
+        for i in range(n):
+            pos = length - n + i
+            page = ind[ip[b] + pos // P]
+            cache[page, 0, :, pos % P] = k[ap[b] + i]
+            cache[page, 1, :, pos % P] = v[ap[b] + i]
+    return cache
 
 
 # ----------------------------------------------------------------------------

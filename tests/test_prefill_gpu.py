@@ -143,3 +143,52 @@ def test_prefill_cfg1_varlen_full_size_sampled():
         check_close(O[k[0], k[1]], ref)
     for b in range(8):
         assert torch.all(O[b, :, int(lens[b]):] == 0)
+
+
+# ---------------------------------------------------------------- LSE output (PF:331-334, unstored there)
+LSE_TOL = 1e-3  # fp32 log-sum-exp of fp32-accumulated scores; exp2 approximations in the kernel
+
+
+@pytest.mark.parametrize("causal", [True, False])
+@pytest.mark.parametrize("S,D,G", [(1, 64, 1), (129, 64, 4), (300, 128, 2), (256, 64, 2)])
+def test_prefill_lse_matches_oracle(causal, S, D, G):
+    from attention_kernel_triton_b200.prefill_flash_attention import flash_attention_prefill_with_lse
+    c = W.make_prefill(B=2, Hq=2 * G, Hkv=2, S=S, D=D, causal=causal, seed=S + D + G)
+    O, LSE = flash_attention_prefill_with_lse(cuda(c.Q), cuda(c.K), cuda(c.V), causal, c.softmax_scale, G)
+    O_plain = flash_attention_prefill(cuda(c.Q), cuda(c.K), cuda(c.V), causal, c.softmax_scale, G)
+    assert torch.equal(O, O_plain)
+    ref = N.prefill_lse_reference(c.Q, c.K, c.V, causal, c.softmax_scale, G)
+    assert LSE.shape == ref.shape and LSE.dtype == torch.float32
+    assert (LSE.cpu() - ref).abs().max().item() <= LSE_TOL
+
+
+def test_prefill_varlen_lse_padding_rows_are_minus_inf():
+    from attention_kernel_triton_b200.prefill_flash_attention_var_len_padding import flash_attention_prefill_with_lse
+    c = W.make_prefill(B=3, Hq=8, Hkv=2, S=300, D=64, causal=True, seed=9)
+    lens = torch.tensor([300, 1, 130], dtype=torch.int32)
+    O, LSE = flash_attention_prefill_with_lse(cuda(c.Q), cuda(c.K), cuda(c.V), True, c.softmax_scale, 4, cuda(lens))
+    ref = N.prefill_lse_reference(c.Q, c.K, c.V, True, c.softmax_scale, 4, lens)
+    fin = torch.isfinite(ref)
+    assert torch.equal(torch.isfinite(LSE.cpu()), fin)
+    assert (LSE.cpu()[fin] - ref[fin]).abs().max().item() <= LSE_TOL
+    check_close(O, N.prefill_varlen_reference(c.Q, c.K, c.V, True, c.softmax_scale, 4, lens))
+
+
+def test_prefill_lse_merges_two_key_halves_like_split_kv():
+    # LSE is what lets partial outputs over disjoint key sets be merged: a non-causal
+    # prefill over keys [0, S/2) and [S/2, S) merged with akt_lse_merge equals the full one
+    from attention_kernel_triton_b200.distributed import lse_merge_into
+    from attention_kernel_triton_b200.prefill_flash_attention import flash_attention_prefill_with_lse
+    c = W.make_prefill(B=1, Hq=4, Hkv=4, S=256, D=64, causal=False, seed=10)
+    Q, K, V = cuda(c.Q), cuda(c.K), cuda(c.V)
+    parts = []
+    for lo, hi in [(0, 128), (128, 256)]:  # the first 128 queries against each half of the keys
+        O_h, L_h = flash_attention_prefill_with_lse(Q[:, :, :128], K[:, :, lo:hi], V[:, :, lo:hi], False,
+                                                    c.softmax_scale, 1)
+        parts.append((O_h.float(), L_h))
+    rows, D = 4 * 128, 64
+    recv = torch.cat([torch.cat([o.reshape(1, -1), l.reshape(1, -1)], dim=1) for o, l in parts], dim=0)
+    out = torch.empty(rows, D, dtype=torch.float16, device=DEV)
+    lse_merge_into(out, recv, rows, D)
+    full = N.prefill_reference(c.Q[:, :, :128], c.K, c.V, False, c.softmax_scale, 1)
+    check_close(out.reshape(1, 4, 128, 64), full)
