@@ -63,11 +63,15 @@ constexpr int kLoadVWarp = 10;     // the V ring (its own warp: two waiting lane
 constexpr int kMmaWarp1 = 11;      // MMA issuer of slot 1 (slot 0: kMmaWarp)
 // Register split: the kernel is compiled for 168 registers per thread (3 warps
 // per SM sub-partition); the producer/MMA warpgroup gives registers back and
-// the softmax warpgroups take them: 2*128*224 + 128*56 <= 384*168.
+// the softmax warpgroups take them: 2*128*216 + 128*64 <= 384*168 (224 and 56
+// for the variant that also writes the log-sum-exp).
 constexpr int kLaunchRegs = 168;
-constexpr int kSoftmaxRegs = 224;
-constexpr int kControlRegs = 56;
-static_assert(2 * 128 * kSoftmaxRegs + 128 * kControlRegs <= kThreads * kLaunchRegs, "register split");
+template <bool LSE>
+struct RegSplit {
+  static constexpr int softmax = LSE ? 224 : 216;
+  static constexpr int control = LSE ? 56 : 64;
+  static_assert(2 * 128 * softmax + 128 * control <= kThreads * kLaunchRegs, "register split");
+};
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 
 // Tile configuration per head_dim D.  Keys per tile BN is chosen so that
@@ -290,7 +294,7 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, vo
 // -------------------------------------------------------------------------
 // kernel
 // -------------------------------------------------------------------------
-template <typename T, int D>
+template <typename T, int D, bool LSE>
 __global__ void __launch_bounds__(kThreads, 1)
     prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                        const __grid_constant__ CUtensorMap tmV, const PrefillParams p) {
@@ -364,7 +368,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   };
 
   if (warp >= 8) {
-  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kControlRegs));
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(RegSplit<LSE>::control));
   if (warp == kLoadWarp || warp == kLoadVWarp) {
     // ========================= TMA producers =========================
     // Phases continue across items: counters are global to the CTA.  Q load n
@@ -493,7 +497,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_wait(mma_idle, 0);
   }
   } else {
-    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kSoftmaxRegs));
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(RegSplit<LSE>::softmax));
     // ========================= softmax warpgroups =========================
     const int t = warp >> 2;                   // slot
     const int r = threadIdx.x & (BM - 1);      // row in the tile = TMEM lane
@@ -517,7 +521,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (row < p.S) {
 #pragma unroll
           for (int c = 0; c < D; c += 8) *reinterpret_cast<uint4*>(orow + c) = make_uint4(0, 0, 0, 0);
-          if (p.lse) p.lse[(int64_t)it.b * p.lse_sb + (int64_t)hq * p.lse_sh + row] = -INFINITY;
+          if constexpr (LSE) p.lse[(int64_t)it.b * p.lse_sb + (int64_t)hq * p.lse_sh + row] = -INFINITY;
         }
         continue;
       }
@@ -621,7 +625,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       pend_inv = has_keys ? 1.f / l : 0.f;
       // LSE in natural log (final once the last tile is exponentiated): the
       // running max is kept in log2 units and P = 2^(x - m)
-      if (p.lse && row < p.S)
+      if (LSE && row < p.S)
         p.lse[(int64_t)it.b * p.lse_sb + (int64_t)hq * p.lse_sh + row] =
             has_keys ? (m_use + __log2f(l)) * kLn2 : -INFINITY;
     }
@@ -684,10 +688,10 @@ int sm_count() {
   return counts[dev];
 }
 
-template <typename T, int D>
+template <typename T, int D, bool LSE>
 int launch_prefill(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const PrefillParams& p,
                    cudaStream_t st) {
-  auto kern = prefill_fwd_kernel<T, D>;
+  auto kern = prefill_fwd_kernel<T, D, LSE>;
   const int smem = (int)Cfg<D>::SMEM;
   // the register split in the kernel is only valid at the compiled count
   static int regs = -1;
@@ -771,10 +775,18 @@ static int prefill_entry(const akt_prefill_args* a, float* lse, int64_t lse_sb, 
   p.lse_sb = lse_sb;
   p.lse_sh = lse_sh;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (lse) {
+    if (a->dtype == AKT_FLOAT16)
+      return a->head_dim == 64 ? launch_prefill<__half, 64, true>(mq, mk, mv, p, st)
+                               : launch_prefill<__half, 128, true>(mq, mk, mv, p, st);
+    return a->head_dim == 64 ? launch_prefill<__nv_bfloat16, 64, true>(mq, mk, mv, p, st)
+                             : launch_prefill<__nv_bfloat16, 128, true>(mq, mk, mv, p, st);
+  }
   if (a->dtype == AKT_FLOAT16)
-    return a->head_dim == 64 ? launch_prefill<__half, 64>(mq, mk, mv, p, st) : launch_prefill<__half, 128>(mq, mk, mv, p, st);
-  return a->head_dim == 64 ? launch_prefill<__nv_bfloat16, 64>(mq, mk, mv, p, st)
-                           : launch_prefill<__nv_bfloat16, 128>(mq, mk, mv, p, st);
+    return a->head_dim == 64 ? launch_prefill<__half, 64, false>(mq, mk, mv, p, st)
+                             : launch_prefill<__half, 128, false>(mq, mk, mv, p, st);
+  return a->head_dim == 64 ? launch_prefill<__nv_bfloat16, 64, false>(mq, mk, mv, p, st)
+                           : launch_prefill<__nv_bfloat16, 128, false>(mq, mk, mv, p, st);
 }
 
 extern "C" int akt_prefill(const akt_prefill_args* a, void* stream) { return prefill_entry(a, nullptr, 0, 0, stream); }
