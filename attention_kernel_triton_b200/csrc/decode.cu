@@ -371,12 +371,15 @@ struct Plan {
   bool direct;
 };
 
-// Tuning knobs, read once per process: AKT_DECODE_STAGE_KB (shared-memory
-// budget of the K/V stage ring per CTA, default 64) and AKT_DECODE_CHUNK_TILES
-// (upper bound on tiles per split-KV chunk, default 128).
+// Tuning knobs, read once per thread: AKT_DECODE_STAGE_KB (shared-memory
+// budget of the K/V stage ring per CTA, default 64), AKT_DECODE_CHUNK_TILES
+// (upper bound on tiles per split-KV chunk, default 128) and
+// AKT_DECODE_ITEMS_PER_SM (work items aimed at per SM, default 3: about one
+// wave at three CTAs per SM; large inputs hit the chunk bound instead).
 int env_int(const char* name, int dflt) {
-  static thread_local int cache_stage = -1, cache_chunk = -1;
-  int* slot = name[11] == 'S' ? &cache_stage : &cache_chunk;
+  static thread_local int cache[3] = {-1, -1, -1};
+  const char k = name[11];
+  int* slot = &cache[k == 'S' ? 0 : k == 'C' ? 1 : 2];
   if (*slot < 0) {
     const char* v = getenv(name);
     const int x = v ? atoi(v) : 0;
@@ -414,8 +417,8 @@ Plan make_plan(bool paged, int B, int Hq, int Hkv, int D, int L, int P, int64_t 
   // (a parity wait is only unambiguous for the current or previous phase).
   const size_t fit = (size_t)env_int("AKT_DECODE_STAGE_KB", 64) * 1024 / stage_bytes;
   pl.num_stages = (int)std::max<size_t>(kConsumerWarps, std::min<size_t>(16, fit / kConsumerWarps * kConsumerWarps));
-  // estimated tiles over all units -> chunk size: aim for ~12 CTAs per SM in
-  // total, but no more than 32 tiles per chunk
+  // estimated tiles over all units -> chunk size: aim for about one wave of
+  // CTAs (3 per SM), but no more than AKT_DECODE_CHUNK_TILES tiles per chunk
   int64_t tiles_per_unit;
   if (paged) {
     tiles_per_unit = num_page_entries * (int64_t)(P / pl.tile_tokens);
@@ -423,7 +426,7 @@ Plan make_plan(bool paged, int B, int Hq, int Hkv, int D, int L, int P, int64_t 
     tiles_per_unit = (int64_t)B * cdiv(L, pl.tile_tokens);
   }
   const int64_t total_tiles = std::max<int64_t>(1, tiles_per_unit * units);
-  const int64_t target = (int64_t)sm_count() * 12;
+  const int64_t target = (int64_t)sm_count() * env_int("AKT_DECODE_ITEMS_PER_SM", 3);
   int64_t ct = (total_tiles + target - 1) / target;
   ct = std::max<int64_t>(1, std::min<int64_t>(env_int("AKT_DECODE_CHUNK_TILES", 128), ct));
   pl.chunk_tokens = (int)(ct * pl.tile_tokens);
