@@ -146,6 +146,16 @@ class AppendPagedArgs(Structure):
     ]
 
 
+AKT_MAX_PEERS = 8
+
+
+class PeerExchange(Structure):
+    _fields_ = [
+        ("peer_data", c_void_p * AKT_MAX_PEERS), ("peer_flags", c_void_p * AKT_MAX_PEERS), ("counter", c_void_p),
+        ("world", c_int32), ("rank", c_int32), ("epoch", ctypes.c_uint32),
+    ]
+
+
 # name -> (restype, argtypes); every function declared in include/akt.h
 SIGNATURES = {
     "akt_abi_version": (c_int, []),
@@ -178,6 +188,13 @@ SIGNATURES = {
     "akt_magicpig_paged_csr": (c_int, [POINTER(SparsePagedArgs), c_void_p, c_int64, c_void_p, c_size_t,
                                        c_void_p]),
     "akt_append_paged_kv": (c_int, [POINTER(AppendPagedArgs), c_void_p]),
+    "akt_ipc_alloc": (c_int, [c_size_t, POINTER(c_void_p), c_void_p]),
+    "akt_ipc_open": (c_int, [c_void_p, POINTER(c_void_p)]),
+    "akt_ipc_close": (c_int, [c_void_p]),
+    "akt_ipc_free": (c_int, [c_void_p]),
+    "akt_sparse_dense_partial_peer": (c_int, [POINTER(SparseDenseArgs), POINTER(PeerExchange), c_void_p, c_size_t,
+                                              c_void_p]),
+    "akt_lse_merge_peer": (c_int, [POINTER(PeerExchange), c_int64, c_int32, c_void_p, c_int64, c_int32, c_void_p]),
     "akt_mask_to_sparse_index": (c_int, [POINTER(MaskToIndexArgs), c_void_p]),
     "akt_sparse_index_to_mask": (c_int, [POINTER(IndexToMaskArgs), c_void_p]),
 }

@@ -74,7 +74,19 @@ struct SparseParams {
   // device's tokens instead of the typed output
   float* out_part_o;
   float* out_part_lse;
+  // peer-store exchange (partial mode): the merge also stores each partial
+  // row into slot `rank` of every device's data area and, when all its CTAs
+  // are done, raises flag `rank` on every device
+  int n_peers, rank;
+  uint32_t epoch;
+  float* peer_data[AKT_MAX_PEERS];
+  uint32_t* peer_flags[AKT_MAX_PEERS];
+  uint32_t* counter;
 };
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
 
 // ---------------------------------------------------------------------------
 // planner: chunks per (batch, unit) = ceil(max nnz over the unit's heads / kCP)
@@ -380,12 +392,35 @@ __global__ void __launch_bounds__(256) sparse_merge_kernel(const SparseParams p)
       }
     }
     const float val = den > 0.f ? num / den : 0.f;
-    if (p.out_part_o) {
+    if (p.n_peers) {
+      const int64_t row = (int64_t)b * p.Hq + head0 + h, rows = (int64_t)p.B * p.Hq;
+      const float lse = den > 0.f ? (M + log2f(den)) * kLn2 : -INFINITY;
+      for (int r = 0; r < p.n_peers; ++r) {
+        float* slot = p.peer_data[r] + (int64_t)p.rank * (rows * D + rows);
+        slot[row * D + d] = val;
+        if (d == 0) slot[rows * D + row] = lse;
+      }
+    } else if (p.out_part_o) {
       const int64_t row = (int64_t)b * p.Hq + head0 + h;
       p.out_part_o[row * D + d] = val;
       if (d == 0) p.out_part_lse[row] = den > 0.f ? (M + log2f(den)) * kLn2 : -INFINITY;
     } else {
       out[(int64_t)b * p.o_sb + (int64_t)(head0 + h) * p.o_sh + (int64_t)d * p.o_sd] = E::from_float(val);
+    }
+  }
+  if (p.n_peers) {
+    // every thread's stores are visible system-wide before this CTA counts
+    // itself done; the last CTA raises the flags (the counter resets for the
+    // next call, which is stream-ordered after this kernel)
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      const unsigned done = atomicAdd(p.counter, 1u) + 1u;
+      if (done == gridDim.x) {
+        __threadfence_system();
+        for (int r = 0; r < p.n_peers; ++r) st_release_sys(p.peer_flags[r] + p.rank, p.epoch);
+        *p.counter = 0u;
+      }
     }
   }
 }
@@ -553,6 +588,10 @@ size_t akt_sparse_dense_workspace_size(const akt_sparse_dense_args* a) {
   return make_sparse_plan(a->batch, a->num_qo_heads, a->num_kv_heads, a->head_dim, a->max_nnz).ws_bytes;
 }
 
+// descriptor of the peer-store exchange for the entry point running on this
+// thread (set only for the duration of akt_sparse_dense_partial_peer)
+static thread_local const akt_peer_exchange* g_peer = nullptr;
+
 static int sparse_dense_entry(const akt_sparse_dense_args* a, void* ws, size_t ws_bytes, void* stream,
                               float* o_part, float* lse_part, const int32_t* csr_ptr = nullptr,
                               int64_t num_inds = 0) {
@@ -578,6 +617,16 @@ static int sparse_dense_entry(const akt_sparse_dense_args* a, void* ws, size_t w
   p.ind = a->sparse_ind; p.ind_sb = a->ind_stride_batch; p.ind_sh = a->ind_stride_head; p.ind_sp = a->ind_stride_pos;
   p.nnz = a->sparse_nnz; p.nnz_sb = a->nnz_stride_batch; p.nnz_sh = a->nnz_stride_head;
   p.csr_ptr = csr_ptr; p.num_inds = num_inds;
+  if (g_peer) {  // akt_sparse_dense_partial_peer
+    p.n_peers = g_peer->world;
+    p.rank = g_peer->rank;
+    p.epoch = g_peer->epoch;
+    p.counter = g_peer->counter;
+    for (int r = 0; r < g_peer->world; ++r) {
+      p.peer_data[r] = g_peer->peer_data[r];
+      p.peer_flags[r] = g_peer->peer_flags[r];
+    }
+  }
   p.out = a->out; p.o_sb = a->out_stride_batch; p.o_sh = a->out_stride_head; p.o_sd = a->out_stride_dim;
   p.B = a->batch; p.Hq = a->num_qo_heads; p.Hkv = a->num_kv_heads; p.L = a->seq_len; p.P = 1;
   p.max_nnz = a->max_nnz;
@@ -611,6 +660,19 @@ int akt_magicpig_paged_csr(const akt_sparse_paged_args* a, const int32_t* sparse
                            size_t ws_bytes, void* stream) {
   if (!sparse_ptr || num_inds < 0) return set_error(AKT_ERR_INVALID, "CSR lists need sparse_ptr and num_inds >= 0");
   return paged_entry(a, ws, ws_bytes, stream, true, nullptr, nullptr, sparse_ptr, num_inds);
+}
+
+int akt_sparse_dense_partial_peer(const akt_sparse_dense_args* a, const akt_peer_exchange* x, void* ws,
+                                  size_t ws_bytes, void* stream) {
+  if (!x || x->world < 1 || x->world > AKT_MAX_PEERS || x->rank < 0 || x->rank >= x->world || !x->counter ||
+      x->epoch == 0)
+    return set_error(AKT_ERR_INVALID, "peer exchange: bad descriptor");
+  for (int r = 0; r < x->world; ++r)
+    if (!x->peer_data[r] || !x->peer_flags[r]) return set_error(AKT_ERR_INVALID, "peer exchange: null peer pointer");
+  g_peer = x;
+  const int rc = sparse_dense_entry(a, ws, ws_bytes, stream, nullptr, nullptr);
+  g_peer = nullptr;
+  return rc;
 }
 
 int akt_sparse_dense_partial(const akt_sparse_dense_args* a, float* o_part, float* lse_part, void* ws,

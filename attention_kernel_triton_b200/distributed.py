@@ -12,12 +12,19 @@ Two layouts, following the structure of the work:
   over NCCL (NVLink) and merged with ``akt_lse_merge``:
   ``O = sum_r e^{lse_r - M} O_r / sum_r e^{lse_r - M}``.
 
-The reference has no multi-GPU code; this is the exchange step BASELINE's
-north star names for the 128K single-sequence case.
+Two implementations of the exchange: ``sparsetoken_decode_kv_split`` calls the
+library all-gather (NCCL); ``PeerKVSplit`` fuses it into the kernels -- the
+sparse kernel's last stage stores each rank's partial straight into every
+peer's exchange region over NVLink (CUDA IPC mappings) and raises a flag, and
+the merge kernel waits on the flags (bounded) and merges locally.
+
+The reference has no multi-GPU code; this is the exchange step the 128K
+single-sequence case needs.
 """
 from __future__ import annotations
 
 import ctypes
+from ctypes import c_void_p
 from typing import Callable, Optional, Tuple
 
 import torch
@@ -107,3 +114,147 @@ def sparsetoken_decode_kv_split(q: torch.Tensor, K_local: torch.Tensor, V_local:
     out = torch.empty((B, Hq, 1, D), dtype=q.dtype, device=q.device)
     (merge_fn or lse_merge_into)(out, recv, rows, D)
     return out
+
+
+# ----------------------------------------------------------------------------
+# exchange fused into the kernels: NVLink peer stores + flags
+# ----------------------------------------------------------------------------
+_HEADER = 256  # flags [2 parities][AKT_MAX_PEERS] uint32 at 0 and 32, completion counter at 64
+
+
+def exchange_layout(rows: int, head_dim: int, world: int):
+    """Byte layout of one device's exchange region: ``(total_bytes, part_floats,
+    data_offset(parity), flags_offset(parity), counter_offset)``.  Data for parity
+    ``p`` is ``[world][rows*head_dim + rows]`` fp32."""
+    part = rows * head_dim + rows
+    total = _HEADER + 2 * world * part * 4
+    return total, part, (lambda p: _HEADER + p * world * part * 4), (lambda p: 4 * _lib.AKT_MAX_PEERS * p), 64
+
+
+class PeerKVSplit:
+    """Sparse-token decode of one sequence split along the key axis across the ranks of
+    ``process_group`` (one GPU each), with the exchange fused into the kernels.
+
+    Built once per shape (it allocates and maps the exchange regions: CUDA IPC handles
+    are all-gathered on the host); each call is one epoch.  Calls must be issued in the
+    same order on every rank, on the current stream.  ``close()`` (collective) unmaps
+    and frees."""
+
+    def __init__(self, B: int, Hq: int, head_dim: int, device, process_group=None):
+        self.pg = process_group
+        self.world = dist.get_world_size(process_group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(process_group) if dist.is_initialized() else 0
+        if self.world > _lib.AKT_MAX_PEERS:
+            raise ValueError(f"at most {_lib.AKT_MAX_PEERS} ranks")
+        self.device = torch.device(device)
+        self.B, self.Hq, self.D = B, Hq, head_dim
+        self.rows = B * Hq
+        total, _, self._data_off, self._flag_off, self._counter_off = exchange_layout(self.rows, head_dim, self.world)
+        L = _lib.lib()
+        ptr, handle = c_void_p(), (ctypes.c_char * 64)()
+        with torch.cuda.device(self.device):
+            _lib.check(L.akt_ipc_alloc(total, ctypes.byref(ptr), handle))
+        self.local = ptr.value
+        handles = [bytes(handle)]
+        if self.world > 1:
+            handles = [None] * self.world
+            dist.all_gather_object(handles, bytes(handle), group=process_group)
+        self.bases = []
+        with torch.cuda.device(self.device):
+            for r in range(self.world):
+                if r == self.rank:
+                    self.bases.append(self.local)
+                    continue
+                h = (ctypes.c_char * 64).from_buffer_copy(handles[r])
+                pp = c_void_p()
+                _lib.check(L.akt_ipc_open(h, ctypes.byref(pp)))
+                self.bases.append(pp.value)
+        self.epoch = 0
+        self._bound = None
+
+    def _descriptor(self, epoch: int):
+        x = _lib.PeerExchange()
+        par = epoch & 1
+        for r, base in enumerate(self.bases):
+            x.peer_data[r] = base + self._data_off(par)
+            x.peer_flags[r] = base + self._flag_off(par)
+        x.counter = self.local + self._counter_off
+        x.world, x.rank, x.epoch = self.world, self.rank, epoch
+        return x
+
+    def __call__(self, q, K_local, V_local, ind_local, nnz_local, softmax_scale: float, GQA_group_size: int):
+        from .sparsetoken_decode_flash_attention_redundant import _sparse_dense_call
+        B, Hq, _, D = q.shape
+        assert (B, Hq, D) == (self.B, self.Hq, self.D), "shape differs from the one this exchange was built for"
+        self.epoch += 1
+        x = self._descriptor(self.epoch)
+        _sparse_dense_call("akt_sparse_dense_partial_peer", None, q, K_local, V_local, ind_local, nnz_local,
+                           softmax_scale, GQA_group_size, peer=x)
+        out = torch.empty((B, Hq, 1, D), dtype=q.dtype, device=q.device)
+        with torch.cuda.device(q.device):
+            _lib.check(_lib.lib().akt_lse_merge_peer(ctypes.byref(x), self.rows, D, out.data_ptr(), D,
+                                                     _lib.dtype_code(out), _lib.stream_ptr(q.device)))
+        return out
+
+    def bind(self, K_local, V_local, ind_local, nnz_local, softmax_scale: float, GQA_group_size: int,
+             dtype=torch.float16):
+        """Fix this rank's key shard and lists for repeated ``step`` calls: the argument
+        structs, scratch and the q / output buffers are built once, so a step is a copy
+        of q and two launches."""
+        L = _lib.lib()
+        dev = self.device
+        ind = _lib.as_int32(ind_local, dev)
+        nnz = _lib.as_int32(nnz_local, dev)
+        q = torch.empty((self.B, self.Hq, 1, self.D), dtype=dtype, device=dev)
+        out = torch.empty_like(q)
+        K, V = K_local, V_local
+        a = _lib.SparseDenseArgs()
+        a.q = q.data_ptr()
+        a.q_stride_batch, a.q_stride_head, a.q_stride_dim = q.stride(0), q.stride(1), q.stride(3)
+        a.k = K.data_ptr()
+        a.k_stride_batch, a.k_stride_head, a.k_stride_token, a.k_stride_dim = K.stride()
+        a.v = V.data_ptr()
+        a.v_stride_batch, a.v_stride_head, a.v_stride_token, a.v_stride_dim = V.stride()
+        (a.ind_stride_batch, a.ind_stride_head, a.ind_stride_pos), (a.nnz_stride_batch, a.nnz_stride_head) = \
+            _lib.index_strides(ind, nnz)
+        a.sparse_ind, a.sparse_nnz = ind.data_ptr(), nnz.data_ptr()
+        a.batch, a.num_qo_heads, a.num_kv_heads, a.seq_len, a.head_dim = self.B, self.Hq, K.shape[1], K.shape[2], self.D
+        a.max_nnz = ind.shape[2]
+        a.dtype = _lib.dtype_code(q)
+        a.softmax_scale = float(softmax_scale)
+        assert self.Hq // K.shape[1] == GQA_group_size
+        ws = _lib.workspace(L.akt_sparse_dense_workspace_size(ctypes.byref(a)), dev)
+        self._bound = {"args": a, "ws": ws, "q": q, "out": out, "keep": (K, V, ind, nnz),
+                       "dtype": _lib.dtype_code(q)}
+
+    def step(self, q):
+        """One decode over the bound shard (``bind`` first); returns the output buffer,
+        which the next step overwrites."""
+        b = self._bound
+        L = _lib.lib()
+        b["q"].copy_(q)
+        self.epoch += 1
+        x = self._descriptor(self.epoch)
+        st = _lib.stream_ptr(self.device)
+        _lib.check(L.akt_sparse_dense_partial_peer(ctypes.byref(b["args"]), ctypes.byref(x), b["ws"].data_ptr(),
+                                                   b["ws"].numel(), st))
+        _lib.check(L.akt_lse_merge_peer(ctypes.byref(x), self.rows, self.D, b["out"].data_ptr(), self.D,
+                                        b["dtype"], st))
+        return b["out"]
+
+    def close(self):
+        """Collective: every rank's kernels are done before any region is unmapped."""
+        if self.bases is None:
+            return
+        torch.cuda.synchronize(self.device)
+        if self.world > 1:
+            dist.barrier(group=self.pg)
+        L = _lib.lib()
+        with torch.cuda.device(self.device):
+            for r, base in enumerate(self.bases):
+                if r != self.rank:
+                    _lib.check(L.akt_ipc_close(c_void_p(base)))
+            if self.world > 1:
+                dist.barrier(group=self.pg)
+            _lib.check(L.akt_ipc_free(c_void_p(self.local)))
+        self.bases = None

@@ -20,7 +20,7 @@ redundant_len = 16  # reference module constant (SD:7)
 
 
 def _sparse_dense_call(entry, out, q, K, V, sparse_ind, sparse_nnz, softmax_scale, GQA_group_size, partial=None,
-                       csr=None):
+                       csr=None, peer=None):
     """Shared launcher; ``partial=(o_part, lse_part)`` selects the partial-output entry point,
     ``csr=(sparse_ptr, max_nnz)`` the CSR-list one (``sparse_ind`` is then the flat index array)."""
     dev = _lib.require_cuda(q, K, V)
@@ -65,6 +65,8 @@ def _sparse_dense_call(entry, out, q, K, V, sparse_ind, sparse_nnz, softmax_scal
                       _lib.stream_ptr(dev))
         if csr is not None:
             return fn(ctypes.byref(a), ptr.data_ptr(), ind.numel(), ws.data_ptr(), ws.numel(), _lib.stream_ptr(dev))
+        if peer is not None:
+            return fn(ctypes.byref(a), ctypes.byref(peer), ws.data_ptr(), ws.numel(), _lib.stream_ptr(dev))
         return fn(ctypes.byref(a), ws.data_ptr(), ws.numel(), _lib.stream_ptr(dev))
 
     def contiguous():

@@ -322,8 +322,28 @@ def kv_split_measurement(dev, pg, world, rank, steps=50):
     t = torch.tensor([e0.elapsed_time(e1) / steps], dtype=torch.float64, device=dev)
     pg.all_reduce(t, op=pg.ReduceOp.MAX)
     ms = float(t[0])
+    # the same split with the exchange fused into the kernels (NVLink peer stores + flags)
+    from attention_kernel_triton_b200.distributed import PeerKVSplit
+    x = PeerKVSplit(1, 32, 128, dev)
+    try:
+        x.bind(K, V, ind, nnz, scale, 4)
+        for _ in range(3):
+            x.step(q)
+        pg.barrier()
+        torch.cuda.synchronize(dev)
+        e0.record()
+        for _ in range(steps):
+            x.step(q)
+        e1.record()
+        torch.cuda.synchronize(dev)
+        tp = torch.tensor([e0.elapsed_time(e1) / steps], dtype=torch.float64, device=dev)
+        pg.all_reduce(tp, op=pg.ReduceOp.MAX)
+    finally:
+        x.close()
+    ms_peer = float(tp[0])
     return {"gbs": total_bytes / ms / 1e6, "ms": ms, "n_gpus": world, "mb": total_bytes / 1e6,
-            "allgather_bytes_per_rank": 32 * (128 + 1) * 4, "steps": steps}
+            "allgather_bytes_per_rank": 32 * (128 + 1) * 4, "steps": steps,
+            "peer_exchange": {"gbs": total_bytes / ms_peer / 1e6, "ms": ms_peer}}
 
 
 def run_ours(args):

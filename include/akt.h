@@ -289,6 +289,43 @@ int akt_lse_merge(const float* o_parts, int64_t o_part_stride, const float* lse_
                   int32_t dtype, void* stream);
 
 /* ------------------------------------------------------------------------ */
+/* KV split with the exchange fused into the kernels (NVLink peer stores)   */
+/* instead of a library all-gather.  Each device owns one exchange region   */
+/* (akt_ipc_alloc: cudaMalloc'd, zeroed, exported as a CUDA IPC handle that */
+/* the other processes map with akt_ipc_open).  Per call (epoch e = 1, 2,   */
+/* ...; parity e & 1 selects one of two buffers so a writer never reaches a */
+/* slot its reader may still be reading):                                   */
+/*  - akt_sparse_dense_partial_peer runs the sparse decode over this        */
+/*    device's tokens and its last kernel stores the fp32 partial           */
+/*    [O (rows x head_dim) | LSE (rows)] into slot `rank` of every device's */
+/*    data area with plain stores, then, once all its CTAs are done, writes */
+/*    e into flag `rank` of every device (system-scope release);            */
+/*  - akt_lse_merge_peer waits (bounded: 2 s, then status 1 and zeros)      */
+/*    until this device's flags all read e, and merges its data area.       */
+/* Only plain stores and loads touch peer memory.  peer_data[r] / peer_flags[r] */
+/* are device r's data area / flag array for this call's parity, as mapped  */
+/* in the calling process; counter is this device's completion counter.     */
+/* ------------------------------------------------------------------------ */
+#define AKT_MAX_PEERS 8
+
+typedef struct akt_peer_exchange {
+  float* peer_data[AKT_MAX_PEERS];     /* [world][rows * head_dim + rows] fp32 each */
+  uint32_t* peer_flags[AKT_MAX_PEERS]; /* [world] each */
+  uint32_t* counter;
+  int32_t world, rank;
+  uint32_t epoch;
+} akt_peer_exchange;
+
+int akt_ipc_alloc(size_t bytes, void** dev_ptr, void* handle_out /* 64 bytes */);
+int akt_ipc_open(const void* handle /* 64 bytes */, void** dev_ptr);
+int akt_ipc_close(void* dev_ptr);
+int akt_ipc_free(void* dev_ptr);
+int akt_sparse_dense_partial_peer(const akt_sparse_dense_args* args, const akt_peer_exchange* x, void* workspace,
+                                  size_t workspace_bytes, void* stream);
+int akt_lse_merge_peer(const akt_peer_exchange* x, int64_t rows, int32_t head_dim, void* out, int64_t out_row_stride,
+                       int32_t dtype, void* stream);
+
+/* ------------------------------------------------------------------------ */
 /* paged KV cache append (write path; no reference counterpart: the         */
 /* reference builds its pools in Python, decode_flash_attention_redundant_  */
 /* var_len_paged.py:337-353)                                                 */

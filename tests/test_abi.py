@@ -53,6 +53,7 @@ STRUCTS = {
     "akt_mask_to_index_args": _lib.MaskToIndexArgs,
     "akt_index_to_mask_args": _lib.IndexToMaskArgs,
     "akt_append_paged_args": _lib.AppendPagedArgs,
+    "akt_peer_exchange": _lib.PeerExchange,
 }
 
 

@@ -16,7 +16,7 @@ from oracle import naive as N
 
 from attention_kernel_triton_b200 import _lib
 from attention_kernel_triton_b200 import workloads as W
-from attention_kernel_triton_b200.distributed import (lse_merge_into, shard_range, shard_sparse_lists,
+from attention_kernel_triton_b200.distributed import (PeerKVSplit, lse_merge_into, shard_range, shard_sparse_lists,
                                                       sparsetoken_decode_kv_split)
 from attention_kernel_triton_b200.sparsetoken_decode_flash_attention_redundant import (
     sparse_dense_partial, sparsetoken_flash_attention_decode)
@@ -127,3 +127,69 @@ def test_kv_split_nccl_two_gpus():
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
     errs = dict(q.get(timeout=5) for _ in range(2))
     assert max(errs.values()) <= TOL, errs
+
+
+def test_peer_exchange_single_device_epochs():
+    # world 1: the kernel publishes into its own region and the merge waits on its own
+    # flag; several epochs exercise both buffer parities and the counter reset
+    c = W.make_sparse_dense(B=1, Hq=32, Hkv=8, L=32768, D=128, keep_p=0.02, seed=31, device=DEV)
+    ref = N.sparsetoken_naive_decode(c.q, c.K, c.V, c.sparse_ind, c.sparse_nnz, c.softmax_scale, c.group)
+    x = PeerKVSplit(1, 32, 128, DEV)
+    try:
+        for _ in range(3):
+            out = x(c.q, c.K, c.V, c.sparse_ind, c.sparse_nnz, c.softmax_scale, c.group)
+            assert (out.float().cpu() - ref).abs().max().item() <= TOL
+        x.bind(c.K, c.V, c.sparse_ind, c.sparse_nnz, c.softmax_scale, c.group)
+        for _ in range(3):
+            assert (x.step(c.q).float().cpu() - ref).abs().max().item() <= TOL
+    finally:
+        x.close()
+    assert _lib.device_status(0) == 0
+
+
+def _peer_worker(rank, world, port, q):
+    import datetime
+
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                            timeout=datetime.timedelta(seconds=60))
+    x = None
+    try:
+        c = W.make_sparse_dense(B=1, Hq=32, Hkv=8, L=32768, D=128, keep_p=0.02, seed=22)  # CPU, same on all ranks
+        lo, hi = shard_range(32768, world, rank)
+        ind, nnz = shard_sparse_lists(c.sparse_ind, c.sparse_nnz, lo, hi)
+        args = (c.q.to(dev), c.K[:, :, lo:hi].contiguous().to(dev), c.V[:, :, lo:hi].contiguous().to(dev),
+                ind.to(dev), nnz.to(dev), c.softmax_scale, c.group)
+        x = PeerKVSplit(1, 32, 128, dev)
+        outs = [x(*args) for _ in range(3)]
+        x.bind(*args[1:])
+        outs += [x.step(args[0]).clone() for _ in range(3)]
+        torch.cuda.synchronize(dev)
+        ref = N.sparsetoken_naive_decode(c.q, c.K, c.V, c.sparse_ind, c.sparse_nnz, c.softmax_scale, c.group)
+        err = max(float((o.float().cpu() - ref).abs().max()) for o in outs)
+        q.put((rank, err, _lib.device_status(rank)))
+    finally:
+        if x is not None:
+            x.close()
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_peer_exchange_two_gpus():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_peer_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=600)
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    res = [q.get(timeout=5) for _ in range(2)]
+    assert max(r[1] for r in res) <= TOL, res
+    assert all(r[2] == 0 for r in res), res
