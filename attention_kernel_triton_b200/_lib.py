@@ -152,7 +152,7 @@ AKT_MAX_PEERS = 8
 class PeerExchange(Structure):
     _fields_ = [
         ("peer_data", c_void_p * AKT_MAX_PEERS), ("peer_flags", c_void_p * AKT_MAX_PEERS), ("counter", c_void_p),
-        ("world", c_int32), ("rank", c_int32), ("epoch", ctypes.c_uint32),
+        ("merge_counter", c_void_p), ("world", c_int32), ("rank", c_int32), ("epoch", ctypes.c_uint32),
     ]
 
 

@@ -49,9 +49,9 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
 // until all `world` flags of this device read `epoch`, then the CTA merges its
 // row from the data area; loads bypass L1 (the area is rewritten remotely).
 template <typename T>
-__global__ void __launch_bounds__(128) lse_merge_peer_kernel(const float* __restrict__ data,
-                                                             const uint32_t* __restrict__ flags, int world,
-                                                             uint32_t epoch, int64_t rows, int D, T* __restrict__ out,
+__global__ void __launch_bounds__(128) lse_merge_peer_kernel(const float* __restrict__ data, uint32_t* flags,
+                                                             uint32_t* merge_counter, int world, uint32_t epoch,
+                                                             int64_t rows, int D, T* __restrict__ out,
                                                              int64_t out_row_stride) {
   __shared__ int ready;
   if (threadIdx.x == 0) {
@@ -86,6 +86,16 @@ __global__ void __launch_bounds__(128) lse_merge_peer_kernel(const float* __rest
     }
     out[row * out_row_stride + d] = Elem<T>::from_float(den > 0.f ? num / den : 0.f);
   }
+  // the last CTA past its wait clears the flags for this parity's next use
+  // (a writer reaches this parity again only after this kernel has finished)
+  if (threadIdx.x == 0) {
+    const unsigned done = atomicAdd(merge_counter, 1u) + 1u;
+    if (done == gridDim.x) {
+      for (int r = 0; r < world; ++r) flags[r] = 0u;
+      *merge_counter = 0u;
+      __threadfence();
+    }
+  }
 }
 }  // namespace
 }  // namespace akt
@@ -95,22 +105,24 @@ using namespace akt;
 extern "C" int akt_lse_merge_peer(const akt_peer_exchange* x, int64_t rows, int32_t head_dim, void* out,
                                   int64_t out_row_stride, int32_t dtype, void* stream) {
   if (!x || x->world < 1 || x->world > AKT_MAX_PEERS || x->rank < 0 || x->rank >= x->world || x->epoch == 0 ||
-      !x->peer_data[x->rank] || !x->peer_flags[x->rank])
+      !x->peer_data[x->rank] || !x->peer_flags[x->rank] || !x->merge_counter)
     return set_error(AKT_ERR_INVALID, "peer exchange: bad descriptor");
   if (rows < 0 || rows > 0x7fffffff || head_dim <= 0) return set_error(AKT_ERR_INVALID, "lse_merge_peer: bad sizes");
   if (dtype != AKT_FLOAT16 && dtype != AKT_BFLOAT16) return set_error(AKT_ERR_INVALID, "dtype");
   if (rows == 0) return AKT_OK;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const float* data = x->peer_data[x->rank];
-  const uint32_t* flags = x->peer_flags[x->rank];
+  uint32_t* flags = x->peer_flags[x->rank];
   {
     ProfileScope prof(st);
     if (dtype == AKT_FLOAT16)
-      lse_merge_peer_kernel<__half><<<(unsigned)rows, 128, 0, st>>>(data, flags, x->world, x->epoch, rows, head_dim,
+      lse_merge_peer_kernel<__half><<<(unsigned)rows, 128, 0, st>>>(data, flags, x->merge_counter, x->world,
+                                                                     x->epoch, rows, head_dim,
                                                                      static_cast<__half*>(out), out_row_stride);
     else
       lse_merge_peer_kernel<__nv_bfloat16><<<(unsigned)rows, 128, 0, st>>>(
-          data, flags, x->world, x->epoch, rows, head_dim, static_cast<__nv_bfloat16*>(out), out_row_stride);
+          data, flags, x->merge_counter, x->world, x->epoch, rows, head_dim, static_cast<__nv_bfloat16*>(out),
+          out_row_stride);
   }
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_error(AKT_ERR_CUDA, std::string("lse_merge_peer: ") + cudaGetErrorString(e));

@@ -119,7 +119,7 @@ def sparsetoken_decode_kv_split(q: torch.Tensor, K_local: torch.Tensor, V_local:
 # ----------------------------------------------------------------------------
 # exchange fused into the kernels: NVLink peer stores + flags
 # ----------------------------------------------------------------------------
-_HEADER = 256  # flags [2 parities][AKT_MAX_PEERS] uint32 at 0 and 32, completion counter at 64
+_HEADER = 256  # flags [2 parities][AKT_MAX_PEERS] uint32 at 0 and 32, completion counters at 64 and 68
 
 
 def exchange_layout(rows: int, head_dim: int, world: int):
@@ -171,15 +171,20 @@ class PeerKVSplit:
                 self.bases.append(pp.value)
         self.epoch = 0
         self._bound = None
+        self._graphs = None
 
-    def _descriptor(self, epoch: int):
+    def _descriptor(self, epoch: int, flag_value: Optional[int] = None):
+        """Exchange descriptor of call ``epoch`` (its parity picks the buffers); the flag
+        value is the epoch itself unless given (graph replays use a constant)."""
         x = _lib.PeerExchange()
         par = epoch & 1
         for r, base in enumerate(self.bases):
             x.peer_data[r] = base + self._data_off(par)
             x.peer_flags[r] = base + self._flag_off(par)
         x.counter = self.local + self._counter_off
-        x.world, x.rank, x.epoch = self.world, self.rank, epoch
+        x.merge_counter = self.local + self._counter_off + 4
+        x.world, x.rank = self.world, self.rank
+        x.epoch = (flag_value if flag_value is not None else epoch) & 0xFFFFFFFF or 1
         return x
 
     def __call__(self, q, K_local, V_local, ind_local, nnz_local, softmax_scale: float, GQA_group_size: int):
@@ -230,22 +235,45 @@ class PeerKVSplit:
     def step(self, q):
         """One decode over the bound shard (``bind`` first); returns the output buffer,
         which the next step overwrites."""
+        self._bound["q"].copy_(q)
+        self.epoch += 1
+        self._launch(self._descriptor(self.epoch))
+        return self._bound["out"]
+
+    def _launch(self, x):
         b = self._bound
         L = _lib.lib()
-        b["q"].copy_(q)
-        self.epoch += 1
-        x = self._descriptor(self.epoch)
         st = _lib.stream_ptr(self.device)
         _lib.check(L.akt_sparse_dense_partial_peer(ctypes.byref(b["args"]), ctypes.byref(x), b["ws"].data_ptr(),
                                                    b["ws"].numel(), st))
         _lib.check(L.akt_lse_merge_peer(ctypes.byref(x), self.rows, self.D, b["out"].data_ptr(), self.D,
                                         b["dtype"], st))
-        return b["out"]
+
+    def capture(self):
+        """Record the bound step as two CUDA graphs, one per buffer parity (flag value 1;
+        the merge clears the flags it consumed, so the same values recur).  Collective in
+        the sense that every rank must then use ``step_graph`` for the same calls."""
+        with torch.cuda.device(self.device):
+            torch.cuda.synchronize(self.device)
+            self._graphs = []
+            for par in (0, 1):
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g):
+                    self._launch(self._descriptor(par, flag_value=1))
+                self._graphs.append(g)
+
+    def step_graph(self, q):
+        """One decode by graph replay (``bind`` and ``capture`` first)."""
+        self._bound["q"].copy_(q)
+        self.epoch += 1
+        self._graphs[self.epoch & 1].replay()
+        return self._bound["out"]
 
     def close(self):
         """Collective: every rank's kernels are done before any region is unmapped."""
         if self.bases is None:
             return
+        self._graphs = None
         torch.cuda.synchronize(self.device)
         if self.world > 1:
             dist.barrier(group=self.pg)

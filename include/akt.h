@@ -301,7 +301,9 @@ int akt_lse_merge(const float* o_parts, int64_t o_part_stride, const float* lse_
 /*    data area with plain stores, then, once all its CTAs are done, writes */
 /*    e into flag `rank` of every device (system-scope release);            */
 /*  - akt_lse_merge_peer waits (bounded: 2 s, then status 1 and zeros)      */
-/*    until this device's flags all read e, and merges its data area.       */
+/*    until this device's flags all read e, merges its data area, and its   */
+/*    last CTA clears those flags, so flag values need not grow and a       */
+/*    captured graph per parity can be replayed.                            */
 /* Only plain stores and loads touch peer memory.  peer_data[r] / peer_flags[r] */
 /* are device r's data area / flag array for this call's parity, as mapped  */
 /* in the calling process; counter is this device's completion counter.     */
@@ -311,9 +313,10 @@ int akt_lse_merge(const float* o_parts, int64_t o_part_stride, const float* lse_
 typedef struct akt_peer_exchange {
   float* peer_data[AKT_MAX_PEERS];     /* [world][rows * head_dim + rows] fp32 each */
   uint32_t* peer_flags[AKT_MAX_PEERS]; /* [world] each */
-  uint32_t* counter;
+  uint32_t* counter;                   /* this device: CTAs of the publishing kernel done */
+  uint32_t* merge_counter;             /* this device: CTAs of the merge done */
   int32_t world, rank;
-  uint32_t epoch;
+  uint32_t epoch;                      /* any non-zero value, the same on every rank */
 } akt_peer_exchange;
 
 int akt_ipc_alloc(size_t bytes, void** dev_ptr, void* handle_out /* 64 bytes */);

@@ -84,7 +84,8 @@ def test_peer_exchange_layout_regions_do_not_overlap():
     for rows, D, world in [(32, 128, 1), (32, 128, 2), (96, 256, 8)]:
         total, part, data_off, flag_off, counter_off = exchange_layout(rows, D, world)
         assert part == rows * D + rows
-        assert flag_off(0) + 4 * 8 <= flag_off(1) and flag_off(1) + 4 * 8 <= counter_off < data_off(0)
+        assert flag_off(0) + 4 * 8 <= flag_off(1) and flag_off(1) + 4 * 8 <= counter_off
+        assert counter_off + 8 <= data_off(0)
         assert data_off(0) + world * part * 4 == data_off(1)
         assert data_off(1) + world * part * 4 == total
         assert data_off(0) % 16 == 0 and data_off(1) % 16 == 0

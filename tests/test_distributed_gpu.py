@@ -142,6 +142,10 @@ def test_peer_exchange_single_device_epochs():
         x.bind(c.K, c.V, c.sparse_ind, c.sparse_nnz, c.softmax_scale, c.group)
         for _ in range(3):
             assert (x.step(c.q).float().cpu() - ref).abs().max().item() <= TOL
+        x.capture()
+        for _ in range(4):  # graph replays alternate the two parities
+            assert (x.step_graph(c.q).float().cpu() - ref).abs().max().item() <= TOL
+        assert (x.step(c.q).float().cpu() - ref).abs().max().item() <= TOL  # eager again after graphs
     finally:
         x.close()
     assert _lib.device_status(0) == 0
@@ -169,6 +173,8 @@ def _peer_worker(rank, world, port, q):
         outs = [x(*args) for _ in range(3)]
         x.bind(*args[1:])
         outs += [x.step(args[0]).clone() for _ in range(3)]
+        x.capture()
+        outs += [x.step_graph(args[0]).clone() for _ in range(4)]
         torch.cuda.synchronize(dev)
         ref = N.sparsetoken_naive_decode(c.q, c.K, c.V, c.sparse_ind, c.sparse_nnz, c.softmax_scale, c.group)
         err = max(float((o.float().cpu() - ref).abs().max()) for o in outs)
