@@ -11,8 +11,9 @@
 // are the new ones.  New token i of sequence b is written at position
 // len_b - n_b + i: row (pos % P) of page indices[indptr[b] + pos / P].
 //
-// One CTA per appended token; its threads copy the token's K and V rows of
-// every kv head in 16-byte vectors (byte work, bound by memory traffic).
+// Each CTA takes 16 consecutive appended tokens: it resolves their
+// destinations in parallel, then copies their K and V rows of every kv head in
+// 16-byte vectors (byte work, bound by memory traffic).
 // Page ids outside the pool, positions outside the sequence and malformed
 // indptrs are skipped and recorded in the device status word.
 #include "common.cuh"
@@ -40,8 +41,11 @@ struct AppendParams {
   int B, Hkv, P, row_bytes;
 };
 
-__global__ void __launch_bounds__(256) append_paged_kernel(const AppendParams p) {
-  const int64_t tok = blockIdx.x;
+constexpr int kTokensPerCta = 16;
+
+// Destination row (K half; V is s_kv further) of appended token `tok`, or null
+// when the page table does not place it (recorded in the status word).
+__device__ __forceinline__ char* append_dst(const AppendParams& p, int64_t tok) {
   // sequence of this appended token: largest b with app_indptr[b] <= tok
   int lo = 0, hi = p.B - 1;
   while (lo < hi) {
@@ -52,27 +56,57 @@ __global__ void __launch_bounds__(256) append_paged_kernel(const AppendParams p)
   const int a0 = __ldg(p.app_indptr + b), a1 = __ldg(p.app_indptr + b + 1);
   const int s = __ldg(p.indptr + b), e = __ldg(p.indptr + b + 1);
   if (a0 > tok || tok >= a1 || s < 0 || e <= s || e > p.num_page_entries) {
-    if (threadIdx.x == 0) record_status(kStatusBadIndptr);
-    return;
+    record_status(kStatusBadIndptr);
+    return nullptr;
   }
   const int last = __ldg(p.last + b);
   const int64_t len = (int64_t)(e - s - 1) * p.P + last;
   const int64_t pos = len - (a1 - a0) + (tok - a0);
   if (last < 1 || last > p.P || pos < 0 || pos >= len) {
-    if (threadIdx.x == 0) record_status(kStatusBadToken);
-    return;
+    record_status(kStatusBadToken);
+    return nullptr;
   }
   const int page = __ldg(p.indices + s + pos / p.P);
   if (page < 0 || page >= p.num_pages) {
-    if (threadIdx.x == 0) record_status(kStatusBadPage);
-    return;
+    record_status(kStatusBadPage);
+    return nullptr;
   }
-  char* dst = p.cache + (int64_t)page * p.s_page + (pos % p.P) * p.s_tok;
-  const int vec = p.row_bytes / 16;  // 16-byte pieces per row
-  for (int w = threadIdx.x; w < 2 * p.Hkv * vec; w += blockDim.x) {
-    const int kv = w / (p.Hkv * vec), r = w - kv * p.Hkv * vec, h = r / vec, c = r - h * vec;
-    const char* src = (kv ? p.v + tok * p.v_tok + h * p.v_head : p.k + tok * p.k_tok + h * p.k_head) + c * 16;
-    *reinterpret_cast<uint4*>(dst + kv * p.s_kv + h * p.s_head + c * 16) = __ldg(reinterpret_cast<const uint4*>(src));
+  return p.cache + (int64_t)page * p.s_page + (pos % p.P) * p.s_tok;
+}
+
+// One CTA per 16 consecutive appended tokens: their destinations are resolved
+// in parallel (one thread each: the lookups are chains of dependent loads),
+// then every thread copies 16-byte pieces of all 16 tokens' rows.
+__global__ void __launch_bounds__(256) append_paged_kernel(const AppendParams p) {
+  __shared__ char* dst_s[kTokensPerCta];
+  const int64_t t0 = (int64_t)blockIdx.x * kTokensPerCta;
+  const int nt = (int)min<int64_t>(kTokensPerCta, p.num_append - t0);
+  if (threadIdx.x < nt) dst_s[threadIdx.x] = append_dst(p, t0 + threadIdx.x);
+  __syncthreads();
+  const int vec = p.row_bytes / 16;          // 16-byte pieces per row
+  const int per_tok = 2 * p.Hkv * vec;       // pieces of one token (K and V, all heads)
+  // four pieces per thread per round: their loads are independent and in flight together
+  const int n = nt * per_tok;
+  for (int w0 = threadIdx.x; w0 < n; w0 += 4 * blockDim.x) {
+    uint4 val[4];
+    char* to[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int w = w0 + u * blockDim.x;
+      to[u] = nullptr;
+      if (w >= n) continue;
+      const int i = w / per_tok, r0 = w - i * per_tok;
+      char* dst = dst_s[i];
+      if (!dst) continue;
+      const int kv = r0 / (p.Hkv * vec), r = r0 - kv * p.Hkv * vec, h = r / vec, c = r - h * vec;
+      const int64_t tok = t0 + i;
+      const char* src = (kv ? p.v + tok * p.v_tok + h * p.v_head : p.k + tok * p.k_tok + h * p.k_head) + c * 16;
+      val[u] = __ldg(reinterpret_cast<const uint4*>(src));
+      to[u] = dst + kv * p.s_kv + h * p.s_head + c * 16;
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+      if (to[u]) *reinterpret_cast<uint4*>(to[u]) = val[u];
   }
 }
 
@@ -122,7 +156,7 @@ extern "C" int akt_append_paged_kv(const akt_append_paged_args* a, void* stream)
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   {
     ProfileScope prof(st);
-    append_paged_kernel<<<(unsigned)a->num_append, 256, 0, st>>>(p);
+    append_paged_kernel<<<(unsigned)((a->num_append + kTokensPerCta - 1) / kTokensPerCta), 256, 0, st>>>(p);
   }
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_error(AKT_ERR_CUDA, std::string("append_paged_kv: ") + cudaGetErrorString(e));
