@@ -80,7 +80,8 @@ __device__ __forceinline__ char* append_dst(const AppendParams& p, int64_t tok) 
 __global__ void __launch_bounds__(256) append_paged_kernel(const AppendParams p) {
   __shared__ char* dst_s[kTokensPerCta];
   const int64_t t0 = (int64_t)blockIdx.x * kTokensPerCta;
-  const int nt = (int)min<int64_t>(kTokensPerCta, p.num_append - t0);
+  const int64_t rest = p.num_append - t0;
+  const int nt = rest < kTokensPerCta ? (int)rest : kTokensPerCta;
   if (threadIdx.x < nt) dst_s[threadIdx.x] = append_dst(p, t0 + threadIdx.x);
   __syncthreads();
   const int vec = p.row_bytes / 16;          // 16-byte pieces per row
