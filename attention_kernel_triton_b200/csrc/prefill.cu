@@ -124,6 +124,15 @@ struct Item {
   int h[kSlots], q0[kSlots], nkv[kSlots];
 };
 
+// The CTA's k-th item: rounds of gridDim.x items in list order, taken left to
+// right in even rounds and right to left in odd ones, so the per-CTA sums of
+// the (descending) item costs stay even; -1 past the end of the list.
+__device__ __forceinline__ int item_of(const PrefillParams& p, int k) {
+  const int g = gridDim.x;
+  const int i = k * g + ((k & 1) ? g - 1 - (int)blockIdx.x : (int)blockIdx.x);
+  return i < p.n_items ? i : -1;
+}
+
 // Item i of the list; every role of the CTA decodes the same item.  Items are
 // ordered by query-tile index, last (longest causal row range) first.
 __device__ __forceinline__ Item decode_item(const PrefillParams& p, int i, int BN) {
@@ -376,7 +385,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (warp == kLoadWarp && lane == 0) {
       uint32_t qn[kSlots] = {0, 0}, gk = 0;
       bool ok = true;
-      for (int i = blockIdx.x; ok && i < p.n_items; i += gridDim.x) {
+      for (int k = 0, i = item_of(p, 0); ok && i >= 0; i = item_of(p, ++k)) {
         const Item it = decode_item(p, i, BN);
 #pragma unroll
         for (int t = 0; t < kSlots; ++t) {
@@ -410,7 +419,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else if (warp == kLoadVWarp && lane == 0) {
       uint32_t gv = 0;
       bool ok = true;
-      for (int i = blockIdx.x; ok && i < p.n_items; i += gridDim.x) {
+      for (int k = 0, i = item_of(p, 0); ok && i >= 0; i = item_of(p, ++k)) {
         const Item it = decode_item(p, i, BN);
         for (int j = 0; j < it.L; ++j, ++gv) {
           const uint32_t st = gv % C::NSV;
@@ -456,7 +465,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       ++gv;
       return true;
     };
-    for (int i = blockIdx.x; ok && i < p.n_items; i += gridDim.x) {
+    for (int k = 0, i = item_of(p, 0); ok && i >= 0; i = item_of(p, ++k)) {
       const Item it = decode_item(p, i, BN);
       const int nkv = t ? it.nkv[1] : it.nkv[0];
       for (int j = 0; ok && j < it.L; ++j) {
@@ -511,7 +520,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     T* pend_orow = nullptr;
     float pend_inv = 0.f;
     bool ok = true, pend_out = false;
-    for (int i = blockIdx.x; ok && i < p.n_items; i += gridDim.x) {
+    for (int k = 0, i = item_of(p, 0); ok && i >= 0; i = item_of(p, ++k)) {
       const Item it = decode_item(p, i, BN);
       // slot fields selected without dynamic indexing (keeps Item in registers)
       const int q0 = t ? it.q0[1] : it.q0[0], hq = t ? it.h[1] : it.h[0], nkv = t ? it.nkv[1] : it.nkv[0];
