@@ -1,4 +1,4 @@
-"""Benchmark of the headline path: paged var-len GQA decode (BASELINE cfg3).
+"""Benchmark of the headline path: paged var-len GQA decode (workload cfg3: B=64, Hq=32, Hkv=8, D=128, P=16).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
@@ -170,7 +170,8 @@ def time_kernels(fn, iters, dev, flush=None):
 
 
 def secondary_measurements(dev, iters=20, only=None):
-    """The other BASELINE configurations, one kernel each (single GPU).
+    """The other benchmark workloads (prefill cfg0/cfg1, decode cfg2 and the long-context
+    sweep, the sparse cfg4 family) and the added paths, one kernel each (single GPU).
     ``only`` restricts the run to one configuration (profiler captures)."""
     from attention_kernel_triton_b200.decode_flash_attention_redundant import flash_attention_decode
     from attention_kernel_triton_b200.magicpig_sparsetoken_decode_flash_attention_redundant_var_len_paged_with_norm import (

@@ -1,7 +1,7 @@
 """GPU parity of the dense and paged decode paths against the CPU oracle and
 the reference's golden outputs.
 
-Tolerance: max-abs <= 2e-3 against the fp32 oracle on
+Tolerance (the parity bar for fp16/bf16 outputs): max-abs <= 2e-3 against the fp32 oracle on
 the same inputs, no NaNs.  For bf16 outputs the output rounding alone is up to
 half a bf16 ulp (2^-9 relative), so bf16 cases allow ``2e-3 + 2^-8 * |ref|``.
 """
@@ -203,7 +203,7 @@ def test_paged_decode_malformed_indptr_is_reported():
     assert not torch.isnan(O).any()
 
 
-# ---------------------------------------------------------------- BASELINE cfg3, full size
+# ---------------------------------------------------------------- cfg3 (B=64, lens U[512, 32768]), full size
 @pytest.fixture(scope="module")
 def cfg3():
     return W.make_paged(seed=0, device=DEV)

@@ -60,7 +60,7 @@ def test_kv_split_emulated_matches_oracle(world):
 
 
 def test_kv_split_128k_single_sequence_over_8_shards():
-    # BASELINE cfg4: 128K-token single sequence, keep 2% per kv head, split over 8 ranks
+    # cfg4 long-context case: 128K-token single sequence, keep 2% per kv head, split over 8 ranks
     c = W.make_sparse_dense(B=1, Hq=32, Hkv=8, L=131072, D=128, keep_p=0.02, seed=12, device=DEV, L_max=4096)
     out = emulate_split(c, 8)
     ref = N.sparsetoken_naive_decode(c.q, c.K, c.V, c.sparse_ind, c.sparse_nnz, c.softmax_scale, c.group)

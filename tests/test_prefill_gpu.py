@@ -109,7 +109,7 @@ def test_prefill_reference_asserts():
         flash_attention_prefill(Q[..., :64], Q[:, :1, :, :64], Q[:, :1, :, :64], True, 0.1, 2)
 
 
-# ---------------------------------------------------------------- BASELINE cfg0 / cfg1, full size
+# ---------------------------------------------------------------- cfg0 / cfg1 (B=8, Hq=64, Hkv=16, S=1024, D=64), full size
 def _sampled_ref(c, heads, varlen=None):
     B, H, S, D = c.Q.shape
     out = {}

@@ -56,7 +56,7 @@ def test_dense_csr_matches_padded_and_golden():
 
 
 def test_dense_csr_cfg4_with_explicit_bound():
-    c = W.make_sparse_dense(seed=41, device=DEV)  # BASELINE cfg4
+    c = W.make_sparse_dense(seed=41, device=DEV)  # cfg4: q [1,32,1,128], K/V [1,8,32000,128], keep 2%
     inds, ptr = sparse_csr_from_lists(c.sparse_ind, c.sparse_nnz)
     O = sparsetoken_flash_attention_decode_csr(c.q, c.K, c.V, inds, ptr, c.softmax_scale, c.group,
                                                max_nnz=c.sparse_ind.shape[2])

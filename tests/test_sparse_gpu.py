@@ -77,7 +77,7 @@ def test_magicpig_matches_reference_golden():
     check_close(O, f["O"])
 
 
-# ---------------------------------------------------------------- BASELINE cfg4 shapes
+# ---------------------------------------------------------------- cfg4 shapes (32000-token dense and 8K-32K paged, keep 2%)
 def test_sparse_dense_cfg4():
     c = W.make_sparse_dense(seed=41)  # q [1,32,1,128], K/V [1,8,32000,128], keep 2% per kv head
     O = sparsetoken_flash_attention_decode(cuda(c.q), cuda(c.K), cuda(c.V), cuda(c.sparse_ind),

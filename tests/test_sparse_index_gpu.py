@@ -97,7 +97,7 @@ def test_lists_to_mask_out_of_range_is_skipped_and_recorded():
 
 
 def test_round_trip_and_decode_through_device_lists():
-    # BASELINE cfg4 shape: keep mask per (kv head, token), p = 0.02, repeated over the group
+    # cfg4 shape (32000 tokens): keep mask per (kv head, token), p = 0.02, repeated over the group
     c = W.make_sparse_dense(B=1, Hq=32, Hkv=8, L=32000, D=128, keep_p=0.02, seed=41, device=DEV)
     mask = N.sparse_mask_from_lists(c.sparse_ind.cpu(), c.sparse_nnz.cpu(), 32000).to(DEV)
     ind, nnz = sparse_index_from_mask(mask, c.sparse_ind.shape[2])
