@@ -428,6 +428,13 @@ Plan make_plan(bool paged, int B, int Hq, int Hkv, int D, int L, int P, int64_t 
   const int64_t total_tiles = std::max<int64_t>(1, tiles_per_unit * units);
   const int64_t target = (int64_t)sm_count() * env_int("AKT_DECODE_ITEMS_PER_SM", 3);
   int64_t ct = (total_tiles + target - 1) / target;
+  if (!paged) {
+    // dense: chunks are cut per (sequence, unit), so size them from the chunks
+    // each one may take (the rounding of a total-based size can add a wave)
+    const int64_t seq_tiles = std::max<int64_t>(1, cdiv(L, pl.tile_tokens));
+    const int64_t per_seq = std::max<int64_t>(1, target / std::max<int64_t>(1, (int64_t)B * units));
+    ct = (seq_tiles + per_seq - 1) / per_seq;
+  }
   ct = std::max<int64_t>(1, std::min<int64_t>(env_int("AKT_DECODE_CHUNK_TILES", 128), ct));
   pl.chunk_tokens = (int)(ct * pl.tile_tokens);
   if (paged) {
