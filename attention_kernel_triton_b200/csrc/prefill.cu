@@ -31,8 +31,11 @@
 // The running max used for exponentiation only moves when the row max grows
 // by more than 8 (log2 units), so O is rescaled rarely (P <= 2^8 stays exact
 // enough in fp16/bf16 relative terms; the final O/l is unchanged).  At
-// head_dim 64 the exponentials bound the kernel: MUFU ex2 delivers 16
-// results per clock per SM, 256 flops of the two MMAs per result.
+// head_dim 64 MUFU ex2 (16 results per clock per SM, 256 flops of the two
+// MMAs per result) is the busiest pipe, but the kernel is bound by its
+// per-tile chain: S MMA -> softmax -> P -> P.V MMA -> next P, with about 100
+// cycles of issue per MMA and about 460 cycles from a commit to the waiting
+// thread; removing every exponential speeds it up by only 11 %.
 // Built without -rdc (whole-program device code): with relocatable device
 // code ptxas ignores setmaxnreg, and the softmax warpgroups need its budget.
 #define AKT_WHOLE_PROGRAM 1
@@ -184,24 +187,43 @@ __host__ __device__ constexpr uint32_t idesc_f16(int fmt, int M, int N, int b_mn
          ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 
-__device__ __forceinline__ void mma_f16(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+// A shared-memory descriptor as its two 32-bit words.  The low word holds the
+// start address in 16-byte units (bits 0-13) and the leading byte offset; the
+// high word the stride byte offset, version and swizzle.  Shared addresses
+// stay below 2^18 bytes, so a tile offset is one add on the low word, which
+// keeps the issuing thread's work per MMA small.
+struct Desc {
+  uint32_t lo, hi;
+};
+
+__device__ __forceinline__ Desc desc_words(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  const uint64_t d = desc_sw128(saddr, lbo, sbo);
+  return Desc{(uint32_t)d, (uint32_t)(d >> 32)};
+}
+
+// A and B from shared memory (descriptor words a_lo/a_hi, b_lo/b_hi)
+__device__ __forceinline__ void mma_f16(uint32_t tmem_d, uint32_t a_lo, uint32_t a_hi, uint32_t b_lo, uint32_t b_hi,
+                                        uint32_t idesc, uint32_t acc) {
   asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-      "l"(a), "l"(b), "r"(idesc), "r"(acc)
+      "{\n\t.reg .pred p;\n\t.reg .b64 da, db;\n\t"
+      "setp.ne.b32 p, %6, 0;\n\t"
+      "mov.b64 da, {%1, %2};\n\t"
+      "mov.b64 db, {%3, %4};\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], da, db, %5, p;\n\t}" ::"r"(tmem_d),
+      "r"(a_lo), "r"(a_hi), "r"(b_lo), "r"(b_hi), "r"(idesc), "r"(acc)
       : "memory");
 }
 
 // A operand from TMEM (K-major, two 16-bit values per 32-bit column, row i
-// in lane i), B from shared memory through its descriptor
-__device__ __forceinline__ void mma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t b, uint32_t idesc,
-                                           uint32_t acc) {
+// in lane i), B from shared memory through its descriptor words
+__device__ __forceinline__ void mma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, uint32_t b_lo, uint32_t b_hi,
+                                           uint32_t idesc, uint32_t acc) {
   asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
-      "r"(tmem_a), "l"(b), "r"(idesc), "r"(acc)
+      "{\n\t.reg .pred p;\n\t.reg .b64 db;\n\t"
+      "setp.ne.b32 p, %5, 0;\n\t"
+      "mov.b64 db, {%2, %3};\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], db, %4, p;\n\t}" ::"r"(tmem_d),
+      "r"(tmem_a), "r"(b_lo), "r"(b_hi), "r"(idesc), "r"(acc)
       : "memory");
 }
 
@@ -259,27 +281,32 @@ __device__ __forceinline__ uint32_t pack_p(float a, float b) {
   return Elem<T>::pack2(a, b);
 }
 
-// Normalised output row of one softmax thread: O (D fp32 TMEM columns at tO)
-// times inv, converted to T and stored at orow (null: rows past S, not stored).
+// O row of one softmax thread (D fp32 TMEM columns at tO) into registers:
+// all loads issued, then one wait.
+template <int D>
+__device__ __forceinline__ void read_o(uint32_t tO, uint32_t (&o)[D / 32][32]) {
+#pragma unroll
+  for (int c = 0; c < D / 32; ++c) tmem_ld32(tO + c * 32, o[c]);
+  tmem_wait_ld();
+}
+
+// Normalised output row: o times inv, converted to T, packed two per word.
 template <typename T, int D>
-__device__ __forceinline__ void write_output(uint32_t tO, T* orow, float inv) {
+__device__ __forceinline__ void pack_o(const uint32_t (&o)[D / 32][32], float inv, uint32_t (&w)[D / 2]) {
 #pragma unroll
-  for (int c = 0; c < D / 32; ++c) {
-    uint32_t rr[32];
-    tmem_ld32(tO + c * 32, rr);
-    tmem_wait_ld();
-    if (orow) {
+  for (int c = 0; c < D / 32; ++c)
 #pragma unroll
-      for (int e = 0; e < 32; e += 8) {
-        uint4 w;
-        w.x = Elem<T>::pack2(__uint_as_float(rr[e + 0]) * inv, __uint_as_float(rr[e + 1]) * inv);
-        w.y = Elem<T>::pack2(__uint_as_float(rr[e + 2]) * inv, __uint_as_float(rr[e + 3]) * inv);
-        w.z = Elem<T>::pack2(__uint_as_float(rr[e + 4]) * inv, __uint_as_float(rr[e + 5]) * inv);
-        w.w = Elem<T>::pack2(__uint_as_float(rr[e + 6]) * inv, __uint_as_float(rr[e + 7]) * inv);
-        *reinterpret_cast<uint4*>(orow + c * 32 + e) = w;
-      }
-    }
-  }
+    for (int e = 0; e < 32; e += 2)
+      w[(c * 32 + e) / 2] = Elem<T>::pack2(__uint_as_float(o[c][e]) * inv, __uint_as_float(o[c][e + 1]) * inv);
+}
+
+// Packed output row to orow (null: rows past S, not stored), 16 bytes a store.
+template <typename T, int D>
+__device__ __forceinline__ void store_o(const uint32_t (&w)[D / 2], T* orow) {
+  if (!orow) return;
+#pragma unroll
+  for (int c = 0; c < D / 8; ++c)
+    reinterpret_cast<uint4*>(orow)[c] = make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
 }
 
 // Slow path of a bounded mbarrier wait: spins on try_wait; every 256 polls it
@@ -444,46 +471,50 @@ __global__ void __launch_bounds__(kThreads, 1)
     // skips.  Per tile: S of tile j, then P.V of tile j-1, so the next S is
     // queued before the tensor core waits on the softmax, also across items.
     const int t = warp == kMmaWarp ? 0 : 1;
-    uint32_t gk = 0, gv = 0, qn = 0, sc = 0, pc = 0;
+    // descriptors of the first Q buffer of this slot and of the first K and V
+    // stages; buffers and k-steps are offsets on the low word
+    const Desc dq = desc_words(smem_u32(smem + C::OFF_Q + t * C::NQ * C::Q_BYTES), 16, 1024);
+    const Desc dk = desc_words(smem_u32(smem + C::OFF_K), 16, 1024);
+    const Desc dv = desc_words(smem_u32(smem + C::OFF_V), BN * 128, 1024);
+    // ring positions as (stage, phase bit), advanced without divisions
+    uint32_t kst = 0, kph = 0, vst = 0, vph = 0, qn = 0, sc = 0, pc = 0;
     bool ok = true;
     bool pend = false, pend_act = false, pend_first = false;  // P.V owed for the previous tile
     auto issue_pv = [&]() -> bool {
-      const uint32_t st = gv % C::NSV;
-      if (!wait(&v_full[st], (gv / C::NSV) & 1)) return false;
+      const uint32_t st = vst;
+      if (!wait(&v_full[st], vph)) return false;
       if (pend_act) {
         if (!wait(&p_full[t], pc & 1)) return false;
         tc_fence_after();
-        const uint32_t sV = smem_u32(smem + C::OFF_V + st * C::KV_BYTES);
+        const uint32_t v_lo = dv.lo + st * (C::KV_BYTES >> 4);
 #pragma unroll
         for (int k = 0; k < BN / 16; ++k)
-          mma_f16_ts(tmem + C::COL_O + t * D, tmem + C::COL_P + t * (BN / 2) + k * 8,
-                     desc_sw128(sV + k * 2048, BN * 128, 1024), IDESC_PV, (!pend_first || k > 0) ? 1u : 0u);
+          mma_f16_ts(tmem + C::COL_O + t * D, tmem + C::COL_P + t * (BN / 2) + k * 8, v_lo + k * (2048 >> 4), dv.hi,
+                     IDESC_PV, (!pend_first || k > 0) ? 1u : 0u);
         mma_commit(&pv_done[t]);
         ++pc;
       }
       mma_commit(&v_empty[st]);
-      ++gv;
+      if (++vst == C::NSV) { vst = 0; vph ^= 1u; }
       return true;
     };
     for (int k = 0, i = item_of(p, 0); ok && i >= 0; i = item_of(p, ++k)) {
       const Item it = decode_item(p, i, BN);
       const int nkv = t ? it.nkv[1] : it.nkv[0];
       for (int j = 0; ok && j < it.L; ++j) {
-        const uint32_t st = gk % C::NSK;
-        if (!wait(&k_full[st], (gk / C::NSK) & 1)) { ok = false; break; }
+        const uint32_t st = kst;
+        if (!wait(&k_full[st], kph)) { ok = false; break; }
         if (j < nkv) {
           const uint32_t qb = qn % C::NQ, use = qn / C::NQ;
           if (j == 0 && !wait(&q_full[t * C::NQ + qb], use & 1)) { ok = false; break; }
           if (sc && !wait(&s_empty[t], (sc - 1) & 1)) { ok = false; break; }
           tc_fence_after();
-          const uint32_t sQ = smem_u32(smem + C::OFF_Q + (t * C::NQ + qb) * C::Q_BYTES);
-          const uint32_t sK = smem_u32(smem + C::OFF_K + st * C::KV_BYTES);
+          const uint32_t q_lo = dq.lo + qb * (C::Q_BYTES >> 4), k_lo = dk.lo + st * (C::KV_BYTES >> 4);
 #pragma unroll
           for (int k = 0; k < D / 16; ++k) {
             const uint32_t offq = (k >> 2) * (BM * 128) + (k & 3) * 32;
             const uint32_t offk = (k >> 2) * (BN * 128) + (k & 3) * 32;
-            mma_f16(tmem + C::COL_S + t * BN, desc_sw128(sQ + offq, 16, 1024), desc_sw128(sK + offk, 16, 1024),
-                    IDESC_S, k > 0);
+            mma_f16(tmem + C::COL_S + t * BN, q_lo + (offq >> 4), dq.hi, k_lo + (offk >> 4), dk.hi, IDESC_S, k > 0);
           }
           mma_commit(&s_full[t]);
           if (j == nkv - 1) {
@@ -493,7 +524,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           ++sc;
         }
         mma_commit(&k_empty[st]);
-        ++gk;
+        if (++kst == C::NSK) { kst = 0; kph ^= 1u; }
         if (pend && !issue_pv()) { ok = false; break; }
         pend = true;
         pend_first = j == 0;
@@ -515,8 +546,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t tO = tmem + lane_addr + C::COL_O + t * D;
     const uint32_t tP = tmem + lane_addr + C::COL_P + t * (BN / 2);
     uint32_t sc = 0, pc = 0, pn = 0;           // S tiles read, P.V completions seen, P tiles written
-    // The output of an item is written after the first tile of the next one
-    // has been exponentiated, so the wait for the item's last P.V is hidden.
+    // The output of an item is read from TMEM after the first tile of the next
+    // one has been exponentiated (so the wait for the item's last P.V is
+    // hidden) and stored to global memory after that tile's P is handed to
+    // the MMA issuer (so the stores are off the P -> P.V path).
     T* pend_orow = nullptr;
     float pend_inv = 0.f;
     bool ok = true, pend_out = false;
@@ -604,10 +637,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           ++pc;
           tc_fence_after();
         }
-        if (j == 0) {
-          if (pend_out) write_output<T, D>(tO, pend_orow, pend_inv);  // previous item, O final
-          pend_out = false;
-        } else if (__any_sync(0xffffffffu, need)) {
+        if (j > 0 && __any_sync(0xffffffffu, need)) {
 #pragma unroll
           for (int c = 0; c < D / 32; ++c) {
             uint32_t rr[32];
@@ -620,11 +650,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
 #pragma unroll
         for (int c = 0; c < BN / 64; ++c) tmem_st32(tP + c * 32, pk[c]);
+        if (j == 0 && pend_out) {
+          uint32_t ob[D / 32][32], ow[D / 2];
+          read_o<D>(tO, ob);
+          pack_o<T, D>(ob, pend_inv, ow);
+          store_o<T, D>(ow, pend_orow);
+        }
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&p_full[t]);
         ++pn;
+        pend_out = false;
       }
       if (!ok) break;
       // O / l for valid rows, zeros for var-len padding rows; rows past S not stored
@@ -641,7 +678,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (ok && pend_out && wait(&pv_done[t], pc & 1)) {
       ++pc;
       tc_fence_after();
-      write_output<T, D>(tO, pend_orow, pend_inv);
+      uint32_t ob[D / 32][32], ow[D / 2];
+      read_o<D>(tO, ob);
+      pack_o<T, D>(ob, pend_inv, ow);
+      store_o<T, D>(ow, pend_orow);
     }
   }
   tc_fence_before();
