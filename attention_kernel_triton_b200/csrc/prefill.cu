@@ -46,6 +46,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <atomic>
 #include <climits>
 #include <cstdlib>
 #include <mutex>
@@ -725,16 +726,18 @@ int make_map(CUtensorMap* m, const void* base, int dtype, int B, int H, int S, i
   return AKT_OK;
 }
 
+// SM count of the current device, cached per device (host threads may race on
+// the first call; each computes the same value)
 int sm_count() {
-  static int counts[64] = {0};
+  static std::atomic<int> counts[64];
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
-  if (!counts[dev]) {
-    int n = 0;
+  int n = counts[dev].load(std::memory_order_relaxed);
+  if (!n) {
     if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
-    counts[dev] = n;
+    counts[dev].store(n, std::memory_order_relaxed);
   }
-  return counts[dev];
+  return n;
 }
 
 template <typename T, int D, bool LSE>
@@ -743,11 +746,11 @@ int launch_prefill(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorM
   auto kern = prefill_fwd_kernel<T, D, LSE>;
   const int smem = (int)Cfg<D>::SMEM;
   // the register split in the kernel is only valid at the compiled count
-  static int regs = -1;
-  if (regs < 0) {
+  // (read once per instantiation; the static's initialisation is thread-safe)
+  static const int regs = [&] {
     cudaFuncAttributes fa;
-    regs = cudaFuncGetAttributes(&fa, kern) == cudaSuccess ? fa.numRegs : 0;
-  }
+    return cudaFuncGetAttributes(&fa, kern) == cudaSuccess ? fa.numRegs : 0;
+  }();
   if (regs != kLaunchRegs)
     return set_error(AKT_ERR_CUDA, "prefill kernel compiled with " + std::to_string(regs) + " registers, expected " +
                                        std::to_string(kLaunchRegs));

@@ -138,7 +138,7 @@ class PeerKVSplit:
     Built once per shape (it allocates and maps the exchange regions: CUDA IPC handles
     are all-gathered on the host); each call is one epoch.  Calls must be issued in the
     same order on every rank, on the current stream.  ``close()`` (collective) unmaps
-    and frees."""
+    and frees; used as a context manager, the exchange closes on exit."""
 
     def __init__(self, B: int, Hq: int, head_dim: int, device, process_group=None):
         self.pg = process_group
@@ -173,6 +173,21 @@ class PeerKVSplit:
         self._bound = None
         self._graphs = None
 
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+        return False
+
+    def _require(self, bound: bool = False, graphs: bool = False):
+        if self.bases is None:
+            raise RuntimeError("PeerKVSplit is closed")
+        if bound and self._bound is None:
+            raise RuntimeError("PeerKVSplit.bind() must come before step()")
+        if graphs and self._graphs is None:
+            raise RuntimeError("PeerKVSplit.capture() must come before step_graph()")
+
     def _descriptor(self, epoch: int, flag_value: Optional[int] = None):
         """Exchange descriptor of call ``epoch`` (its parity picks the buffers); the flag
         value is the epoch itself unless given (graph replays use a constant)."""
@@ -189,6 +204,7 @@ class PeerKVSplit:
 
     def __call__(self, q, K_local, V_local, ind_local, nnz_local, softmax_scale: float, GQA_group_size: int):
         from .sparsetoken_decode_flash_attention_redundant import _sparse_dense_call
+        self._require()
         B, Hq, _, D = q.shape
         assert (B, Hq, D) == (self.B, self.Hq, self.D), "shape differs from the one this exchange was built for"
         self.epoch += 1
@@ -206,6 +222,10 @@ class PeerKVSplit:
         """Fix this rank's key shard and lists for repeated ``step`` calls: the argument
         structs, scratch and the q / output buffers are built once, so a step is a copy
         of q and two launches."""
+        self._require()
+        assert K_local.dim() == 4 and K_local.shape[0] == self.B and K_local.shape[3] == self.D, \
+            "K shard must be [B, Hkv, L_local, D] with this exchange's B and head_dim"
+        assert V_local.shape == K_local.shape, "V shard must match the K shard"
         L = _lib.lib()
         dev = self.device
         ind = _lib.as_int32(ind_local, dev)
@@ -235,6 +255,7 @@ class PeerKVSplit:
     def step(self, q):
         """One decode over the bound shard (``bind`` first); returns the output buffer,
         which the next step overwrites."""
+        self._require(bound=True)
         self._bound["q"].copy_(q)
         self.epoch += 1
         self._launch(self._descriptor(self.epoch))
@@ -253,6 +274,7 @@ class PeerKVSplit:
         """Record the bound step as two CUDA graphs, one per buffer parity (flag value 1;
         the merge clears the flags it consumed, so the same values recur).  Collective in
         the sense that every rank must then use ``step_graph`` for the same calls."""
+        self._require(bound=True)
         with torch.cuda.device(self.device):
             torch.cuda.synchronize(self.device)
             self._graphs = []
@@ -264,6 +286,7 @@ class PeerKVSplit:
 
     def step_graph(self, q):
         """One decode by graph replay (``bind`` and ``capture`` first)."""
+        self._require(bound=True, graphs=True)
         self._bound["q"].copy_(q)
         self.epoch += 1
         self._graphs[self.epoch & 1].replay()

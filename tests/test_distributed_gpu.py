@@ -151,6 +151,23 @@ def test_peer_exchange_single_device_epochs():
     assert _lib.device_status(0) == 0
 
 
+def test_peer_exchange_call_order_is_checked():
+    c = W.make_sparse_dense(B=1, Hq=8, Hkv=2, L=2048, D=128, keep_p=0.05, seed=32, device=DEV)
+    with PeerKVSplit(1, 8, 128, DEV) as x:
+        with pytest.raises(RuntimeError, match="bind"):
+            x.step(c.q)
+        with pytest.raises(AssertionError, match="head_dim"):
+            x.bind(c.K[..., :64], c.V[..., :64], c.sparse_ind, c.sparse_nnz, c.softmax_scale, c.group)
+        x.bind(c.K, c.V, c.sparse_ind, c.sparse_nnz, c.softmax_scale, c.group)
+        with pytest.raises(RuntimeError, match="capture"):
+            x.step_graph(c.q)
+        ref = N.sparsetoken_naive_decode(c.q, c.K, c.V, c.sparse_ind, c.sparse_nnz, c.softmax_scale, c.group)
+        assert (x.step(c.q).float().cpu() - ref).abs().max().item() <= TOL
+    with pytest.raises(RuntimeError, match="closed"):
+        x.step(c.q)
+    assert _lib.device_status(0) == 0
+
+
 def _peer_worker(rank, world, port, q):
     import datetime
 
