@@ -426,7 +426,12 @@ Plan make_plan(bool paged, int B, int Hq, int Hkv, int D, int L, int P, int64_t 
     tiles_per_unit = (int64_t)B * cdiv(L, pl.tile_tokens);
   }
   const int64_t total_tiles = std::max<int64_t>(1, tiles_per_unit * units);
-  const int64_t target = (int64_t)sm_count() * env_int("AKT_DECODE_ITEMS_PER_SM", 3);
+  // work items aimed at per SM: three, or two for dense inputs whose (sequence,
+  // unit) pairs alone are at least half an SM count (each pair then needs few
+  // chunks, and longer ones amortise a CTA's start-up and the merge)
+  const int ips_env = env_int("AKT_DECODE_ITEMS_PER_SM", 0);
+  const int ips = ips_env > 0 ? ips_env : (!paged && 2 * (int64_t)B * units >= sm_count() ? 2 : 3);
+  const int64_t target = (int64_t)sm_count() * ips;
   int64_t ct = (total_tiles + target - 1) / target;
   if (!paged) {
     // dense: chunks are cut per (sequence, unit), so size them from the chunks
