@@ -188,4 +188,24 @@ constexpr float kLn2 = 0.6931471805599453f;
 
 __host__ __device__ constexpr int cdiv(int a, int b) { return (a + b - 1) / b; }
 
+// n / d for 32-bit unsigned n by multiply-high and shift (the round-up
+// multiplier method of Granlund and Montgomery, "Division by invariant
+// integers using multiplication", PLDI 1994): l = ceil(log2 d),
+// m = floor(2^32 (2^l - d) / d) + 1, n / d = (umulhi(n, m) + n) >> l with a
+// 33-bit sum.  Built on the host for a divisor 1 <= d < 2^31.
+struct FastDiv {
+  uint32_t d, m, l;
+};
+
+inline FastDiv make_fastdiv(uint32_t d) {
+  uint32_t l = 0;
+  while (l < 32 && (1ull << l) < d) ++l;
+  const uint64_t m = ((1ull << 32) * ((1ull << l) - d)) / d + 1;
+  return FastDiv{d, (uint32_t)m, l};
+}
+
+__device__ __forceinline__ uint32_t fdiv(uint32_t n, const FastDiv& f) {
+  return (uint32_t)(((uint64_t)__umulhi(n, f.m) + n) >> f.l);
+}
+
 }  // namespace akt

@@ -39,6 +39,9 @@ struct AppendParams {
   const int32_t* app_indptr;
   int64_t num_append;
   int B, Hkv, P, row_bytes;
+  FastDiv div_tok;   // 16-byte pieces of one token (K and V, all heads)
+  FastDiv div_half;  // pieces of one token's K (or V) rows
+  FastDiv div_row;   // pieces of one row
 };
 
 constexpr int kTokensPerCta = 16;
@@ -84,10 +87,8 @@ __global__ void __launch_bounds__(256) append_paged_kernel(const AppendParams p)
   const int nt = rest < kTokensPerCta ? (int)rest : kTokensPerCta;
   if (threadIdx.x < nt) dst_s[threadIdx.x] = append_dst(p, t0 + threadIdx.x);
   __syncthreads();
-  const int vec = p.row_bytes / 16;          // 16-byte pieces per row
-  const int per_tok = 2 * p.Hkv * vec;       // pieces of one token (K and V, all heads)
   // four pieces per thread per round: their loads are independent and in flight together
-  const int n = nt * per_tok;
+  const int n = nt * (int)p.div_tok.d;
   for (int w0 = threadIdx.x; w0 < n; w0 += 4 * blockDim.x) {
     uint4 val[4];
     char* to[4];
@@ -96,10 +97,12 @@ __global__ void __launch_bounds__(256) append_paged_kernel(const AppendParams p)
       const int w = w0 + u * blockDim.x;
       to[u] = nullptr;
       if (w >= n) continue;
-      const int i = w / per_tok, r0 = w - i * per_tok;
+      // piece -> (token, K or V, head, 16-byte column) by multiply-shift division
+      const int i = (int)fdiv((uint32_t)w, p.div_tok), r0 = w - i * (int)p.div_tok.d;
       char* dst = dst_s[i];
       if (!dst) continue;
-      const int kv = r0 / (p.Hkv * vec), r = r0 - kv * p.Hkv * vec, h = r / vec, c = r - h * vec;
+      const int kv = (int)fdiv((uint32_t)r0, p.div_half), r = r0 - kv * (int)p.div_half.d;
+      const int h = (int)fdiv((uint32_t)r, p.div_row), c = r - h * (int)p.div_row.d;
       const int64_t tok = t0 + i;
       const char* src = (kv ? p.v + tok * p.v_tok + h * p.v_head : p.k + tok * p.k_tok + h * p.k_head) + c * 16;
       val[u] = __ldg(reinterpret_cast<const uint4*>(src));
@@ -154,6 +157,12 @@ extern "C" int akt_append_paged_kv(const akt_append_paged_args* a, void* stream)
   p.Hkv = a->num_kv_heads;
   p.P = a->page_size;
   p.row_bytes = a->head_dim * 2;
+  const int vec = p.row_bytes / 16;  // 16-byte pieces per row
+  if ((int64_t)2 * p.Hkv * vec * kTokensPerCta > 0x7fffffff)
+    return set_error(AKT_ERR_UNSUPPORTED, "append_paged_kv: token rows too large");
+  p.div_tok = make_fastdiv((uint32_t)(2 * p.Hkv * vec));
+  p.div_half = make_fastdiv((uint32_t)(p.Hkv * vec));
+  p.div_row = make_fastdiv((uint32_t)vec);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   {
     ProfileScope prof(st);
