@@ -431,7 +431,7 @@ def run_ours(args):
     h_out = torch.empty((args.batch, 32, 128), dtype=torch.float16).pin_memory()
     h2d = sum(x.numel() * x.element_size() for x in (h_q, h_indptr, h_indices, h_last))
     d2h = h_out.numel() * h_out.element_size()
-    e2e_steps = max(3, min(args.steps, 200))
+    e2e_steps = max(3, args.steps)  # as many steps as the device-timed loop
     compute = torch.cuda.current_stream(dev)
     copier = torch.cuda.Stream(dev)
     hosts = (h_q, h_indptr, h_indices, h_last)
