@@ -164,6 +164,7 @@ __global__ void __launch_bounds__(kDecodeThreads, (G * D > 512) ? 2 : 3) decode_
   const int unit = item - cg * p.units;
   int b, c, seq_len;
   if (PAGED) {
+    grid_dep_wait();  // chunk offsets come from the planner kernel
     const int total = p.chunk_offset[p.B];
     if (cg >= total) return;
     int lo = 0, hi = p.B - 1;  // largest b with chunk_offset[b] <= cg
@@ -306,6 +307,7 @@ __global__ void __launch_bounds__(kDecodeThreads, (G * D > 512) ? 2 : 3) decode_
 template <typename T, int D, int G, bool PAGED>
 __global__ void __launch_bounds__(256) decode_merge_kernel(const DecodeParams p) {
   using E = Elem<T>;
+  grid_dep_wait();  // partials (and chunk offsets) of the previous kernels
   const int b = blockIdx.x / p.units;
   const int unit = blockIdx.x - b * p.units;
   int c0, c1;
@@ -475,11 +477,16 @@ int launch_decode(DecodeParams p, const Plan& pl, cudaStream_t st) {
   if (PAGED) paged_plan_kernel<<<1, 1024, 0, st>>>(p);
   if (pl.items > 0) {
     ProfileScope prof(st);
-    kern<<<(unsigned)pl.items, kDecodeThreads, pl.smem, st>>>(p);
+    if (PAGED)  // after the planner: may start while it runs
+      e = launch_dependent(kern, dim3((unsigned)pl.items), dim3(kDecodeThreads), pl.smem, st, p);
+    else
+      kern<<<(unsigned)pl.items, kDecodeThreads, pl.smem, st>>>(p);
+    if (e != cudaSuccess) return set_error(AKT_ERR_CUDA, std::string("decode launch: ") + cudaGetErrorString(e));
   }
   if (!pl.direct) {
     const unsigned nb = (unsigned)p.B * p.units;
-    if (nb > 0) decode_merge_kernel<T, D, G, PAGED><<<nb, 256, 0, st>>>(p);
+    if (nb > 0) e = launch_dependent(decode_merge_kernel<T, D, G, PAGED>, dim3(nb), dim3(256), 0, st, p);
+    if (e != cudaSuccess) return set_error(AKT_ERR_CUDA, std::string("decode merge launch: ") + cudaGetErrorString(e));
   }
   e = cudaGetLastError();
   if (e != cudaSuccess) return set_error(AKT_ERR_CUDA, std::string("decode launch: ") + cudaGetErrorString(e));

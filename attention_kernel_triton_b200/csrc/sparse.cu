@@ -326,6 +326,7 @@ __global__ void __launch_bounds__(kSThreads) sparse_decode_kernel(const SparsePa
     fence_mbar_init();
   }
   __syncthreads();
+  grid_dep_wait();  // item offsets come from the planner kernel
   const int n_units = p.B * p.units;
   const int total = p.unit_offset[n_units];
   for (int item = blockIdx.x; item < total; item += gridDim.x) {
@@ -373,6 +374,7 @@ __global__ void __launch_bounds__(kSThreads) sparse_decode_kernel(const SparsePa
 template <typename T, int D, int G>
 __global__ void __launch_bounds__(256) sparse_merge_kernel(const SparseParams p) {
   using E = Elem<T>;
+  grid_dep_wait();  // partials (and item offsets) of the previous kernels
   const int u = blockIdx.x;
   const int b = u / p.units, unit = u - b * p.units;
   const int kvh = unit / p.g_tiles;
@@ -474,10 +476,12 @@ int launch_sparse(const SparseParams& p, const SparsePlan& pl, cudaStream_t st) 
   sparse_plan_kernel<G><<<1, 1024, 0, st>>>(p);
   if (pl.items > 0) {
     ProfileScope prof(st);
-    kern<<<pl.grid, kSThreads, smem, st>>>(p);
+    e = launch_dependent(kern, dim3(pl.grid), dim3(kSThreads), smem, st, p);
+    if (e != cudaSuccess) return set_error(AKT_ERR_CUDA, std::string("sparse launch: ") + cudaGetErrorString(e));
   }
   const unsigned nb = (unsigned)(p.B * p.units);
-  if (nb > 0) sparse_merge_kernel<T, D, G><<<nb, 256, 0, st>>>(p);
+  if (nb > 0) e = launch_dependent(sparse_merge_kernel<T, D, G>, dim3(nb), dim3(256), 0, st, p);
+  if (e != cudaSuccess) return set_error(AKT_ERR_CUDA, std::string("sparse merge launch: ") + cudaGetErrorString(e));
   e = cudaGetLastError();
   if (e != cudaSuccess) return set_error(AKT_ERR_CUDA, std::string("sparse launch: ") + cudaGetErrorString(e));
   return AKT_OK;
