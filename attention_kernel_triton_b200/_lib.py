@@ -6,6 +6,7 @@ entry point raises ``RuntimeError`` -- there is no fallback path.
 """
 from __future__ import annotations
 
+import contextlib
 import ctypes
 import os
 import threading
@@ -240,8 +241,23 @@ def dtype_code(t: torch.Tensor) -> int:
     raise TypeError(f"unsupported dtype {t.dtype}: float16 or bfloat16 expected")
 
 
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
 def stream_ptr(device: torch.device) -> int:
+    """torch's current stream on ``device`` as a ``cudaStream_t`` value (the raw
+    query when torch has it: it skips building a Stream object per call)."""
+    if _raw_stream is not None:
+        return _raw_stream(device.index if device.index is not None else torch.cuda.current_device())
     return torch.cuda.current_stream(device).cuda_stream
+
+
+def on_device(device: torch.device):
+    """Context that makes ``device`` current for the launches inside it; no
+    device switch (and no context-manager cost) when it already is."""
+    if device.index is None or device.index == torch.cuda.current_device():
+        return contextlib.nullcontext()
+    return torch.cuda.device(device)
 
 
 def workspace(nbytes: int, device: torch.device) -> torch.Tensor:

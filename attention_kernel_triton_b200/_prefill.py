@@ -54,6 +54,6 @@ def prefill_into(O, Q, K, V, causal, softmax_scale, GQA_group_size, varlen=None,
         for k in t:
             t[k] = t[k].contiguous()
 
-    with torch.cuda.device(dev):
+    with _lib.on_device(dev):
         _lib.run_with_layout_retry(call, contiguous)
     return O

@@ -7,6 +7,8 @@
 #include <cuda_bf16.h>
 #include <stdint.h>
 
+#include <atomic>
+
 #include "../../include/akt.h"
 
 namespace akt {
@@ -50,6 +52,25 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
 
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+// Raise kernel Kern's dynamic shared-memory limit on the current device to at
+// least `bytes`.  The driver call is made only when the value already set
+// for this kernel and device is smaller (one static per kernel instantiation).
+template <auto Kern>
+cudaError_t ensure_smem_limit(size_t bytes) {
+  static std::atomic<int> set[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
+    return cudaFuncSetAttribute(Kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+  if (set[dev].load(std::memory_order_relaxed) >= (int)bytes) return cudaSuccess;
+  const cudaError_t e = cudaFuncSetAttribute(Kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+  if (e == cudaSuccess) {
+    int cur = set[dev].load(std::memory_order_relaxed);
+    while (cur < (int)bytes && !set[dev].compare_exchange_weak(cur, (int)bytes, std::memory_order_relaxed)) {
+    }
+  }
+  return e;
 }
 
 // Programmatic dependent launch.  A kernel launched by launch_dependent() may

@@ -472,7 +472,7 @@ Plan make_plan(bool paged, int B, int Hq, int Hkv, int D, int L, int P, int64_t 
 template <typename T, int D, int G, bool PAGED>
 int launch_decode(DecodeParams p, const Plan& pl, cudaStream_t st) {
   auto kern = decode_splitkv_kernel<T, D, G, PAGED>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl.smem);
+  cudaError_t e = ensure_smem_limit<decode_splitkv_kernel<T, D, G, PAGED>>(pl.smem);
   if (e != cudaSuccess) return set_error(AKT_ERR_CUDA, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
   if (PAGED) paged_plan_kernel<<<1, 1024, 0, st>>>(p);
   if (pl.items > 0) {

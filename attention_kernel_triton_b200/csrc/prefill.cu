@@ -754,7 +754,7 @@ int launch_prefill(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorM
   if (regs != kLaunchRegs)
     return set_error(AKT_ERR_CUDA, "prefill kernel compiled with " + std::to_string(regs) + " registers, expected " +
                                        std::to_string(kLaunchRegs));
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  cudaError_t e = ensure_smem_limit<prefill_fwd_kernel<T, D, LSE>>((size_t)smem);
   if (e != cudaSuccess) return set_error(AKT_ERR_CUDA, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
   const int grid = std::min(p.n_items, sm_count());  // persistent: one CTA per SM
   {

@@ -471,7 +471,7 @@ template <typename T, int D, int G, bool PAGED, bool MAGIC>
 int launch_sparse(const SparseParams& p, const SparsePlan& pl, cudaStream_t st) {
   auto kern = sparse_decode_kernel<T, D, G, PAGED, MAGIC>;
   const size_t smem = SparseSmem<T, D, G>::bytes;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  cudaError_t e = ensure_smem_limit<sparse_decode_kernel<T, D, G, PAGED, MAGIC>>(smem);
   if (e != cudaSuccess) return set_error(AKT_ERR_CUDA, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
   sparse_plan_kernel<G><<<1, 1024, 0, st>>>(p);
   if (pl.items > 0) {

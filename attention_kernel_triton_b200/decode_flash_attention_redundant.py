@@ -43,7 +43,7 @@ def decode_dense_into(out, q, K, V, softmax_scale):
         raise TypeError("q, K, V and the output must share one dtype")
     L = _lib.lib()
     qq, KK, VV = q, K, V
-    with torch.cuda.device(dev):
+    with _lib.on_device(dev):
         for attempt in range(2):
             a = _dense_args(qq, KK, VV, out, softmax_scale)
             ws = _lib.workspace(L.akt_decode_dense_workspace_size(ctypes.byref(a)), dev)

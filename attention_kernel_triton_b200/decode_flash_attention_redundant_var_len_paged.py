@@ -73,7 +73,7 @@ def decode_paged_into(out, q, paged_kv_cache, kv_page_indptr, kv_page_indices, k
     qq = q if q.stride(3) == 1 else q.contiguous()
     cache = paged_kv_cache
     L = _lib.lib()
-    with torch.cuda.device(dev):
+    with _lib.on_device(dev):
         for attempt in range(2):
             a = _paged_args(qq, cache, indptr, indices, last, out, scale)
             ws = _lib.workspace(L.akt_decode_paged_workspace_size(ctypes.byref(a)), dev)

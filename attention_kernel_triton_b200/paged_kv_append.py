@@ -48,6 +48,6 @@ def append_paged_kv_cache(paged_kv_cache, append_k, append_v, append_indptr, kv_
     a.append_indptr, a.num_append = app.data_ptr(), k.shape[0]
     a.batch, a.num_kv_heads, a.page_size, a.head_dim = B, Hkv, P, D
     a.dtype = _lib.dtype_code(k)
-    with torch.cuda.device(dev):
+    with _lib.on_device(dev):
         _lib.check(_lib.lib().akt_append_paged_kv(ctypes.byref(a), _lib.stream_ptr(dev)))
     return paged_kv_cache

@@ -73,7 +73,7 @@ def _sparse_dense_call(entry, out, q, K, V, sparse_ind, sparse_nnz, softmax_scal
         for k in t:
             t[k] = t[k].contiguous()
 
-    with torch.cuda.device(dev):
+    with _lib.on_device(dev):
         _lib.run_with_layout_retry(call, contiguous)
 
 

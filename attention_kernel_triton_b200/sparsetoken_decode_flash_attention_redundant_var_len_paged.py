@@ -79,7 +79,7 @@ def sparse_paged_call(entry, out, q, paged_kv_cache, kv_page_indptr, kv_page_ind
     def contiguous():
         t["q"], t["cache"] = t["q"].contiguous(), t["cache"].contiguous()
 
-    with torch.cuda.device(dev):
+    with _lib.on_device(dev):
         _lib.run_with_layout_retry(call, contiguous)
     return out
 
