@@ -78,6 +78,30 @@ struct RegSplit {
 };
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 
+// Var-len work order (shared memory, built by every CTA in its prologue from
+// the per-sequence lengths).  With padding, a query tile past its sequence's
+// length costs nothing, and the plain order (query-tile index, then batch)
+// scatters those free items among the real ones, so the per-CTA sums of item
+// costs come out uneven.  Here the list is grouped into levels, one per
+// query-tile index from the last down (the causal cost of a real item is its
+// tile index + 1): level l holds the real items of the batches that reach
+// tile qt = n_q_tiles - 1 - l, the longest sequences first (perm); every free
+// item follows all real ones, in the same level order.
+// The order is a compile-time variant (SCHED), used only by var-len calls that
+// fit the table: the other kernels compile exactly as without it (extra item
+// setup code in the softmax warps' region, at 216 registers, measured 9 %
+// slower on the causal prefill even where it never ran).  The table is kept
+// small (2.3 KB), so D=64 stays inside the 164 KB shared-memory carveout.
+constexpr int kSchedMaxB = 256;      // batches the table holds
+constexpr int kSchedMaxTiles = 128;  // query tiles per sequence the table holds (S <= 16384)
+struct VarlenSched {
+  int32_t vstart[kSchedMaxTiles + 1];  // first real item of level l
+  int32_t zstart[kSchedMaxTiles + 1];  // first free item of level l, counted after the last real item
+  int16_t cnt[kSchedMaxTiles];         // batches with a real tile at level l
+  int16_t perm[kSchedMaxB];            // batches by query-tile count, descending (ties by index)
+  int16_t ntiles[kSchedMaxB];          // query tiles holding rows of each sequence
+};
+
 // Tile configuration per head_dim D.  Keys per tile BN is chosen so that
 // S[2], O[2] and P[2] fit the 512 TMEM columns of one SM:
 //   D=64 : BN=128 -> 256 + 128 + 128 = 512 columns; smem 64 KB Q + 3-stage K, V rings = 160 KB
@@ -105,7 +129,12 @@ struct Cfg {
   static constexpr int N_BARS = 2 * kSlots * NQ + 2 * NSK + 2 * NSV + 4 * kSlots + 1;
   static constexpr uint32_t BAR_BYTES = (N_BARS * 8 + 8 + 15) / 16 * 16;
   static constexpr uint32_t SMEM = OFF_BAR + BAR_BYTES;  // base is 1024-aligned
-  static_assert(SMEM <= 227 * 1024, "shared memory budget");
+  // the var-len order table follows, in the kernels that use it
+  static constexpr uint32_t OFF_SCHED = SMEM;
+  static constexpr uint32_t SMEM_SCHED = SMEM + sizeof(VarlenSched);
+  static_assert(SMEM_SCHED <= 227 * 1024, "shared memory budget");
+  // with the 1 KB the driver reserves per CTA, D=64 fits the 164 KB carveout
+  static_assert(D != 64 || SMEM_SCHED + 1024 <= 164 * 1024, "D=64 shared-memory carveout");
 };
 
 struct PrefillParams {
@@ -139,13 +168,82 @@ __device__ __forceinline__ int item_of(const PrefillParams& p, int k) {
 
 // Item i of the list; every role of the CTA decodes the same item.  Items are
 // ordered by query-tile index, last (longest causal row range) first.
-__device__ __forceinline__ Item decode_item(const PrefillParams& p, int i, int BN) {
+// Level of item i in a table of level starts (st[0] = 0 <= i < st[n]): the l
+// with st[l] <= i < st[l + 1].  A linear scan (few live registers: the
+// producer and MMA warps decode every item with 56-64 registers); at most
+// n_q_tiles steps, against an item of up to n_q_tiles key tiles.
+__device__ __forceinline__ int sched_level(const int32_t* st, int i) {
+  int l = 0;
+  while (st[l + 1] <= i) ++l;
+  return l;
+}
+
+// Fills the var-len order table (all threads of the CTA; the caller's next
+// __syncthreads publishes the prefix sums thread 0 writes last).
+__device__ __forceinline__ void build_sched(const PrefillParams& p, VarlenSched* vs) {
+  for (int b = threadIdx.x; b < p.B; b += blockDim.x) {
+    const int len = min(max(__ldg(p.varlen + b), 0), p.S);
+    vs->ntiles[b] = (int16_t)((len + BM - 1) / BM);
+  }
+  __syncthreads();
+  for (int b = threadIdx.x; b < p.B; b += blockDim.x) {
+    const int nb = vs->ntiles[b];
+    int rank = 0;
+    for (int o = 0; o < p.B; ++o) {
+      const int no = vs->ntiles[o];
+      rank += (no > nb || (no == nb && o < b)) ? 1 : 0;
+    }
+    vs->perm[rank] = (int16_t)b;
+  }
+  for (int l = threadIdx.x; l < p.n_q_tiles; l += blockDim.x) {
+    const int qt = p.n_q_tiles - 1 - l;
+    int c = 0;
+    for (int o = 0; o < p.B; ++o) c += vs->ntiles[o] > qt ? 1 : 0;
+    vs->cnt[l] = (int16_t)c;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const int hp_n = p.Hq / 2;
+    int v = 0, z = 0;
+    for (int l = 0; l < p.n_q_tiles; ++l) {
+      vs->vstart[l] = v;
+      vs->zstart[l] = z;
+      v += vs->cnt[l] * hp_n;
+      z += (p.B - vs->cnt[l]) * hp_n;
+    }
+    vs->vstart[p.n_q_tiles] = v;
+    vs->zstart[p.n_q_tiles] = z;
+  }
+}
+
+template <bool SCHED>
+__device__ __forceinline__ Item decode_item(const PrefillParams& p, const VarlenSched* vs, int i, int BN) {
   Item it;
   if (p.pair_heads) {
-    const int hp_n = p.Hq / 2, per = p.B * hp_n;
-    const int qt = p.n_q_tiles - 1 - i / per, r = i % per;
-    it.b = r / hp_n;
-    const int hp = r % hp_n;
+    const int hp_n = p.Hq / 2;
+    int qt, hp;
+    if constexpr (SCHED) {
+      const int vtot = vs->vstart[p.n_q_tiles];
+      int l, r, first;
+      if (i < vtot) {
+        l = sched_level(vs->vstart, i);
+        r = i - vs->vstart[l];
+        first = 0;
+      } else {
+        l = sched_level(vs->zstart, i - vtot);
+        r = i - vtot - vs->zstart[l];
+        first = vs->cnt[l];
+      }
+      qt = p.n_q_tiles - 1 - l;
+      it.b = vs->perm[first + r / hp_n];
+      hp = r % hp_n;
+    } else {
+      const int per = p.B * hp_n;
+      qt = p.n_q_tiles - 1 - i / per;
+      const int r = i % per;
+      it.b = r / hp_n;
+      hp = r % hp_n;
+    }
     it.h[0] = 2 * hp;
     it.h[1] = 2 * hp + 1;
     it.q0[0] = it.q0[1] = qt * BM;
@@ -331,7 +429,7 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, vo
 // -------------------------------------------------------------------------
 // kernel
 // -------------------------------------------------------------------------
-template <typename T, int D, bool LSE>
+template <typename T, int D, bool LSE, bool SCHED>
 __global__ void __launch_bounds__(kThreads, 1)
     prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                        const __grid_constant__ CUtensorMap tmV, const PrefillParams p) {
@@ -346,6 +444,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (threadIdx.x == 0) record_status(kStatusWaitTimeout);
     return;
   }
+  if constexpr (SCHED) build_sched(p, reinterpret_cast<VarlenSched*>(smem + C::OFF_SCHED));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
   uint64_t* q_full = bars;                       // [slot][NQ]
   uint64_t* q_empty = q_full + kSlots * C::NQ;   // [slot][NQ]
@@ -414,7 +513,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t qn[kSlots] = {0, 0}, gk = 0;
       bool ok = true;
       for (int k = 0, i = item_of(p, 0); ok && i >= 0; i = item_of(p, ++k)) {
-        const Item it = decode_item(p, i, BN);
+        const Item it = decode_item<SCHED>(p, reinterpret_cast<const VarlenSched*>(smem + C::OFF_SCHED), i, BN);
 #pragma unroll
         for (int t = 0; t < kSlots; ++t) {
           if (!it.nkv[t]) continue;
@@ -448,7 +547,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t gv = 0;
       bool ok = true;
       for (int k = 0, i = item_of(p, 0); ok && i >= 0; i = item_of(p, ++k)) {
-        const Item it = decode_item(p, i, BN);
+        const Item it = decode_item<SCHED>(p, reinterpret_cast<const VarlenSched*>(smem + C::OFF_SCHED), i, BN);
         for (int j = 0; j < it.L; ++j, ++gv) {
           const uint32_t st = gv % C::NSV;
           if (gv >= C::NSV && !wait(&v_empty[st], ((gv / C::NSV) - 1) & 1)) { ok = false; break; }
@@ -500,7 +599,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       return true;
     };
     for (int k = 0, i = item_of(p, 0); ok && i >= 0; i = item_of(p, ++k)) {
-      const Item it = decode_item(p, i, BN);
+      const Item it = decode_item<SCHED>(p, reinterpret_cast<const VarlenSched*>(smem + C::OFF_SCHED), i, BN);
       const int nkv = t ? it.nkv[1] : it.nkv[0];
       for (int j = 0; ok && j < it.L; ++j) {
         const uint32_t st = kst;
@@ -555,7 +654,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     float pend_inv = 0.f;
     bool ok = true, pend_out = false;
     for (int k = 0, i = item_of(p, 0); ok && i >= 0; i = item_of(p, ++k)) {
-      const Item it = decode_item(p, i, BN);
+      const Item it = decode_item<SCHED>(p, reinterpret_cast<const VarlenSched*>(smem + C::OFF_SCHED), i, BN);
       // slot fields selected without dynamic indexing (keeps Item in registers)
       const int q0 = t ? it.q0[1] : it.q0[0], hq = t ? it.h[1] : it.h[0], nkv = t ? it.nkv[1] : it.nkv[0];
       const int row = q0 + r;
@@ -740,11 +839,11 @@ int sm_count() {
   return n;
 }
 
-template <typename T, int D, bool LSE>
+template <typename T, int D, bool LSE, bool SCHED>
 int launch_prefill(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const PrefillParams& p,
                    cudaStream_t st) {
-  auto kern = prefill_fwd_kernel<T, D, LSE>;
-  const int smem = (int)Cfg<D>::SMEM;
+  auto kern = prefill_fwd_kernel<T, D, LSE, SCHED>;
+  const int smem = (int)(SCHED ? Cfg<D>::SMEM_SCHED : Cfg<D>::SMEM);
   // the register split in the kernel is only valid at the compiled count
   // (read once per instantiation; the static's initialisation is thread-safe)
   static const int regs = [&] {
@@ -754,7 +853,7 @@ int launch_prefill(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorM
   if (regs != kLaunchRegs)
     return set_error(AKT_ERR_CUDA, "prefill kernel compiled with " + std::to_string(regs) + " registers, expected " +
                                        std::to_string(kLaunchRegs));
-  cudaError_t e = ensure_smem_limit<prefill_fwd_kernel<T, D, LSE>>((size_t)smem);
+  cudaError_t e = ensure_smem_limit<prefill_fwd_kernel<T, D, LSE, SCHED>>((size_t)smem);
   if (e != cudaSuccess) return set_error(AKT_ERR_CUDA, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
   const int grid = std::min(p.n_items, sm_count());  // persistent: one CTA per SM
   {
@@ -764,6 +863,15 @@ int launch_prefill(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorM
   e = cudaGetLastError();
   if (e != cudaSuccess) return set_error(AKT_ERR_CUDA, std::string("prefill launch: ") + cudaGetErrorString(e));
   return AKT_OK;
+}
+
+// the kernel variant for the output (LSE or not) and the work order
+template <typename T, int D>
+int dispatch_prefill(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const PrefillParams& p,
+                     bool lse, bool sched, cudaStream_t st) {
+  if (lse)
+    return sched ? launch_prefill<T, D, true, true>(mq, mk, mv, p, st) : launch_prefill<T, D, true, false>(mq, mk, mv, p, st);
+  return sched ? launch_prefill<T, D, false, true>(mq, mk, mv, p, st) : launch_prefill<T, D, false, false>(mq, mk, mv, p, st);
 }
 
 bool al16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; }
@@ -827,18 +935,14 @@ static int prefill_entry(const akt_prefill_args* a, float* lse, int64_t lse_sb, 
   p.lse_sb = lse_sb;
   p.lse_sh = lse_sh;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (lse) {
-    if (a->dtype == AKT_FLOAT16)
-      return a->head_dim == 64 ? launch_prefill<__half, 64, true>(mq, mk, mv, p, st)
-                               : launch_prefill<__half, 128, true>(mq, mk, mv, p, st);
-    return a->head_dim == 64 ? launch_prefill<__nv_bfloat16, 64, true>(mq, mk, mv, p, st)
-                             : launch_prefill<__nv_bfloat16, 128, true>(mq, mk, mv, p, st);
-  }
+  // var-len work order from the lengths when the table holds the batch (any
+  // other call keeps the plain order)
+  const bool sched = p.varlen && p.pair_heads && p.B <= kSchedMaxB && p.n_q_tiles <= kSchedMaxTiles;
   if (a->dtype == AKT_FLOAT16)
-    return a->head_dim == 64 ? launch_prefill<__half, 64, false>(mq, mk, mv, p, st)
-                             : launch_prefill<__half, 128, false>(mq, mk, mv, p, st);
-  return a->head_dim == 64 ? launch_prefill<__nv_bfloat16, 64, false>(mq, mk, mv, p, st)
-                           : launch_prefill<__nv_bfloat16, 128, false>(mq, mk, mv, p, st);
+    return a->head_dim == 64 ? dispatch_prefill<__half, 64>(mq, mk, mv, p, lse != nullptr, sched, st)
+                             : dispatch_prefill<__half, 128>(mq, mk, mv, p, lse != nullptr, sched, st);
+  return a->head_dim == 64 ? dispatch_prefill<__nv_bfloat16, 64>(mq, mk, mv, p, lse != nullptr, sched, st)
+                           : dispatch_prefill<__nv_bfloat16, 128>(mq, mk, mv, p, lse != nullptr, sched, st);
 }
 
 extern "C" int akt_prefill(const akt_prefill_args* a, void* stream) { return prefill_entry(a, nullptr, 0, 0, stream); }

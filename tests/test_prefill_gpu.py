@@ -93,6 +93,28 @@ def test_prefill_varlen_shapes(causal):
     check_close(O, N.prefill_varlen_reference(c.Q, c.K, c.V, causal, c.softmax_scale, 4, lens))
 
 
+# The var-len kernel orders its work from the lengths (real query tiles by
+# causal cost, then the tiles past each sequence's length); these cases cover
+# zero-length and one-row sequences, ties, D=128, an odd group (one query head
+# per item, plain order) and more batches than the order table holds (plain
+# order).  Output is independent of the order, so all match the oracle.
+@pytest.mark.parametrize("B,Hq,Hkv,S,D,lens", [
+    (6, 8, 2, 384, 64, [0, 384, 5, 384, 250, 128]),
+    (5, 8, 2, 300, 128, [300, 0, 77, 299, 1]),
+    (4, 6, 2, 256, 64, [256, 0, 129, 40]),
+    (257, 2, 1, 64, 64, None),
+])
+def test_prefill_varlen_work_order(B, Hq, Hkv, S, D, lens):
+    c = W.make_prefill(B=B, Hq=Hq, Hkv=Hkv, S=S, D=D, causal=True, seed=21)
+    if lens is None:
+        g = torch.Generator().manual_seed(22)
+        lens = torch.randint(0, S + 1, (B,), generator=g, dtype=torch.int64).tolist()
+    lens = torch.tensor(lens, dtype=torch.int32)
+    G = Hq // Hkv
+    O = flash_attention_prefill_varlen(cuda(c.Q), cuda(c.K), cuda(c.V), True, c.softmax_scale, G, cuda(lens))
+    check_close(O, N.prefill_varlen_reference(c.Q, c.K, c.V, True, c.softmax_scale, G, lens))
+
+
 def test_prefill_strided_inputs():
     c = W.make_prefill(B=2, Hq=4, Hkv=2, S=150, D=64, causal=True, seed=8)
     Qt = cuda(c.Q).transpose(1, 2).contiguous().transpose(1, 2)   # [B,H,S,D] view, token-major storage
