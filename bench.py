@@ -270,6 +270,43 @@ def secondary_measurements(dev, iters=20, only=None):
             return {"gbs": nbytes / ms / 1e6, "ms": ms, "mb": nbytes / 1e6, "l2": "flushed"}
         return run
 
+    def torch_sdpa_cfg0(backend):
+        """Context, not the product: torch's own scaled_dot_product_attention on
+        the cfg0 inputs through one library backend (K/V expanded to the 64
+        query heads outside the timed region), timed with CUDA events around
+        the call; a 1 ms device sleep ahead of each call keeps the host's
+        dispatch time out of the events.  Null when the backend refuses the
+        inputs."""
+        def run():
+            import torch.nn.functional as F
+            from torch.nn.attention import SDPBackend, sdpa_kernel
+            c = W.make_prefill(seed=0, device=dev)
+            Ke = c.K.repeat_interleave(c.group, dim=1)
+            Ve = c.V.repeat_interleave(c.group, dim=1)
+            be = {"cudnn": SDPBackend.CUDNN_ATTENTION, "flash": SDPBackend.FLASH_ATTENTION}[backend]
+
+            def fn():
+                with sdpa_kernel([be]):
+                    return F.scaled_dot_product_attention(c.Q, Ke, Ve, is_causal=True, scale=c.softmax_scale)
+            try:
+                fn()
+            except RuntimeError as e:
+                return {"tflops": None, "error": str(e).splitlines()[0][:160]}
+            for _ in range(3):
+                fn()
+            ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(iters)]
+            for a, b in ev:
+                flush.zero_()
+                torch.cuda._sleep(2_000_000)  # ~1 ms at 1.9 GHz
+                a.record()
+                fn()
+                b.record()
+            torch.cuda.synchronize(dev)
+            ms = sum(a.elapsed_time(b) for a, b in ev) / iters
+            return {"tflops": c.flops / ms / 1e9, "ms": ms, "frac_of_bf16_peak": c.flops / ms / 1e9 / tf,
+                    "backend": backend, "l2": "flushed", "note": "library reference for context; not this repo's kernel"}
+        return run
+
     table = [
         ("prefill_cfg0_causal", prefill_cfg0),
         ("prefill_cfg1_varlen", prefill_cfg1),
@@ -285,6 +322,8 @@ def secondary_measurements(dev, iters=20, only=None):
         ("append_paged_cfg0_kv", append_cfg0),
         ("mask_to_index_cfg4", mask_to_index(32000, 3840)),
         ("mask_to_index_128k", mask_to_index(131072, 4096)),
+        ("context_torch_sdpa_cudnn_cfg0", torch_sdpa_cfg0("cudnn")),
+        ("context_torch_sdpa_flash_cfg0", torch_sdpa_cfg0("flash")),
     ]
     out = {}
     for name, fn in table:
