@@ -185,7 +185,7 @@ template <typename T, int D, int G>
 struct SparseSmem {
   static constexpr size_t kv = (size_t)2 * kCP * D * sizeof(T);
   static constexpr size_t comb = sizeof(float) * ((size_t)kSW * G * (2 + D) + (size_t)kSW * kRowsPerSubTile * G);
-  static constexpr size_t idx = sizeof(int) * ((size_t)G * kCP + G);
+  static constexpr size_t idx = sizeof(int) * ((size_t)G * kCP + G + 4);
   static constexpr size_t flags = 64;  // kCP row-valid bytes, padded
   static constexpr size_t bytes = kv + comb + idx + flags + 16;
 };
@@ -199,6 +199,7 @@ struct SparseCta {
   float *comb_m, *comb_l, *comb_o, *p_s;
   int* idx_s;
   int* nnz_s;
+  int* item_s;  // [0] unit, [1] chunk of the current item, [2..3] indptr[b], indptr[b + 1]
   unsigned char* ok_s;
   uint64_t* bar;
   int tid, warp, lane;
@@ -214,7 +215,8 @@ struct SparseCta {
     p_s = comb_o + kSW * G * D;
     idx_s = reinterpret_cast<int*>(p_s + kSW * kRowsPerSubTile * G);
     nnz_s = idx_s + G * kCP;
-    ok_s = reinterpret_cast<unsigned char*>(nnz_s + G);
+    item_s = nnz_s + G;
+    ok_s = reinterpret_cast<unsigned char*>(item_s + 4);
     bar = reinterpret_cast<uint64_t*>((reinterpret_cast<uintptr_t>(ok_s + 64) + 7) & ~uintptr_t(7));
     tid = threadIdx.x;
     warp = tid >> 5;
@@ -232,7 +234,7 @@ struct SparseCta {
       const int tok = rows[tid];
       if (tok >= 0) {
         if (PAGED) {
-          const int s = p.indptr[b], e = p.indptr[b + 1];
+          const int s = item_s[2], e = item_s[3];  // indptr[b], indptr[b + 1]
           const int npg = e - s;
           if (s < 0 || npg < 0 || e > p.num_page_entries || tok >= npg * p.P) {
             record_status(kStatusBadToken);
@@ -330,28 +332,63 @@ __global__ void __launch_bounds__(kSThreads) sparse_decode_kernel(const SparsePa
   const int n_units = p.B * p.units;
   const int total = p.unit_offset[n_units];
   for (int item = blockIdx.x; item < total; item += gridDim.x) {
-    int lo = 0, hi = n_units - 1;  // largest u with unit_offset[u] <= item
-    while (lo < hi) {
-      const int mid = (lo + hi + 1) >> 1;
-      if (p.unit_offset[mid] <= item) lo = mid; else hi = mid - 1;
+    // The item's unit u: the one with unit_offset[u] <= item < unit_offset[u + 1].
+    // Up to kSThreads units: one round of independent loads, one thread per
+    // unit (exactly one matches; units with no items have equal bounds).
+    // More units: binary search.  The loads that follow are issued together
+    // where they do not depend on each other: each is a round trip to memory,
+    // and one item per CTA (short lists) is a handful of them end to end.
+    if (n_units <= kSThreads) {
+      if (cta.tid < n_units) {
+        const int a = p.unit_offset[cta.tid], z = p.unit_offset[cta.tid + 1];
+        if (a <= item && item < z) {
+          cta.item_s[0] = cta.tid;
+          cta.item_s[1] = item - a;
+        }
+      }
+    } else if (cta.tid == 0) {
+      int lo = 0, hi = n_units - 1;  // largest u with unit_offset[u] <= item
+      while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (p.unit_offset[mid] <= item) lo = mid; else hi = mid - 1;
+      }
+      cta.item_s[0] = lo;
+      cta.item_s[1] = item - p.unit_offset[lo];
     }
-    const int u = lo;
-    const int c = item - p.unit_offset[u];
+    __syncthreads();
+    const int u = cta.item_s[0];
+    const int c = cta.item_s[1];
     const int b = u / p.units, unit = u - b * p.units;
     const int kvh = unit / p.g_tiles;
     const int head0 = kvh * p.group + (unit - kvh * p.g_tiles) * G;
     const int p0 = c * kCP;
+    // round 1: nnz (CSR: row offsets), the page range (paged) and, for padded
+    // lists, the list entries themselves (positions < max_nnz exist; those
+    // at or past nnz are masked once nnz is known)
     if (cta.tid < G) cta.nnz_s[cta.tid] = clamped_nnz(p, b, head0 + cta.tid);
+    if (PAGED && cta.tid == G) {
+      cta.item_s[2] = p.indptr[b];
+      cta.item_s[3] = p.indptr[b + 1];
+    }
+    if (!p.csr_ptr) {
+      for (int e = cta.tid; e < G * kCP; e += kSThreads) {
+        const int h = e / kCP, j = e - h * kCP;
+        const int pos = p0 + j;
+        cta.idx_s[e] = pos < p.max_nnz
+                           ? p.ind[(int64_t)b * p.ind_sb + (int64_t)(head0 + h) * p.ind_sh + (int64_t)pos * p.ind_sp]
+                           : -1;
+      }
+    }
     __syncthreads();
+    // round 2: CSR entries (their row offset is checked by clamped_nnz, nnz 0
+    // if malformed); padded entries past nnz masked (each thread its own)
     for (int e = cta.tid; e < G * kCP; e += kSThreads) {
       const int h = e / kCP, j = e - h * kCP;
       const int pos = p0 + j;
       if (pos >= cta.nnz_s[h])
         cta.idx_s[e] = -1;
-      else if (p.csr_ptr)  // row offset checked by clamped_nnz (nnz 0 if malformed)
+      else if (p.csr_ptr)
         cta.idx_s[e] = p.ind[(int64_t)__ldg(p.csr_ptr + (int64_t)b * p.Hq + head0 + h) + pos];
-      else
-        cta.idx_s[e] = p.ind[(int64_t)b * p.ind_sb + (int64_t)(head0 + h) * p.ind_sh + (int64_t)pos * p.ind_sp];
     }
     __syncthreads();
     bool same = true;
@@ -434,7 +471,6 @@ struct SparsePlan {
   int G_tile, units;
   int64_t items;  // upper bound
   size_t smem, ws_bytes, off_lse, off_units;
-  int grid;
 };
 
 int sparse_group_tile(int group, int D) {
@@ -463,7 +499,6 @@ SparsePlan make_sparse_plan(int B, int Hq, int Hkv, int D, int max_nnz) {
   pl.off_units = ws;
   ws += al256(((size_t)B * pl.units + 1) * sizeof(int));
   pl.ws_bytes = ws;
-  pl.grid = (int)std::max<int64_t>(1, std::min<int64_t>(pl.items, (int64_t)sm_count() * 8));
   return pl;
 }
 
@@ -473,10 +508,19 @@ int launch_sparse(const SparseParams& p, const SparsePlan& pl, cudaStream_t st) 
   const size_t smem = SparseSmem<T, D, G>::bytes;
   cudaError_t e = ensure_smem_limit<sparse_decode_kernel<T, D, G, PAGED, MAGIC>>(smem);
   if (e != cudaSuccess) return set_error(AKT_ERR_CUDA, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
+  // One resident wave of CTAs walks the items (the count is an upper bound
+  // from the list capacity; the planner finds the real one on the device).
+  // CTAs beyond what fits would wait for a second wave, mostly to find no
+  // item.  Residency per SM is read once per instantiation.
+  static const int resident = [&] {
+    int n = 0;
+    return cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, kSThreads, smem) == cudaSuccess && n > 0 ? n : 1;
+  }();
+  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(pl.items, (int64_t)sm_count() * resident));
   sparse_plan_kernel<G><<<1, 1024, 0, st>>>(p);
   if (pl.items > 0) {
     ProfileScope prof(st);
-    e = launch_dependent(kern, dim3(pl.grid), dim3(kSThreads), smem, st, p);
+    e = launch_dependent(kern, dim3(grid), dim3(kSThreads), smem, st, p);
     if (e != cudaSuccess) return set_error(AKT_ERR_CUDA, std::string("sparse launch: ") + cudaGetErrorString(e));
   }
   const unsigned nb = (unsigned)(p.B * p.units);
