@@ -83,23 +83,24 @@ constexpr float kRescaleThreshold = 8.0f;  // log2 units
 // length costs nothing, and the plain order (query-tile index, then batch)
 // scatters those free items among the real ones, so the per-CTA sums of item
 // costs come out uneven.  Here the list is grouped into levels, one per
-// query-tile index from the last down (the causal cost of a real item is its
-// tile index + 1): level l holds the real items of the batches that reach
-// tile qt = n_q_tiles - 1 - l, the longest sequences first (perm); every free
-// item follows all real ones, in the same level order.
+// query-tile index (paired heads) or pair of query tiles (one head per item),
+// from the last down; the causal cost of a real item grows with its level.
+// Level l holds the real items of the batches that reach it, the longest
+// sequences first (perm); every free item follows all real ones, in the same
+// level order.
 // The order is a compile-time variant (SCHED), used only by var-len calls that
 // fit the table: the other kernels compile exactly as without it (extra item
 // setup code in the softmax warps' region, at 216 registers, measured 9 %
 // slower on the causal prefill even where it never ran).  The table is kept
 // small (2.3 KB), so D=64 stays inside the 164 KB shared-memory carveout.
 constexpr int kSchedMaxB = 256;      // batches the table holds
-constexpr int kSchedMaxTiles = 128;  // query tiles per sequence the table holds (S <= 16384)
+constexpr int kSchedMaxTiles = 128;  // levels the table holds (S <= 16384, or 32768 with one head per item)
 struct VarlenSched {
   int32_t vstart[kSchedMaxTiles + 1];  // first real item of level l
   int32_t zstart[kSchedMaxTiles + 1];  // first free item of level l, counted after the last real item
-  int16_t cnt[kSchedMaxTiles];         // batches with a real tile at level l
-  int16_t perm[kSchedMaxB];            // batches by query-tile count, descending (ties by index)
-  int16_t ntiles[kSchedMaxB];          // query tiles holding rows of each sequence
+  int16_t cnt[kSchedMaxTiles];         // batches with a real item at level l
+  int16_t perm[kSchedMaxB];            // batches by levels reached, descending (ties by index)
+  int16_t ntiles[kSchedMaxB];          // levels each sequence reaches (its query tiles, or tile pairs)
 };
 
 // Tile configuration per head_dim D.  Keys per tile BN is chosen so that
@@ -180,10 +181,19 @@ __device__ __forceinline__ int sched_level(const int32_t* st, int i) {
 
 // Fills the var-len order table (all threads of the CTA; the caller's next
 // __syncthreads publishes the prefix sums thread 0 writes last).
+// Levels of the order: query tiles (paired heads) or pairs of consecutive
+// query tiles (one head per item); the items of a (level, batch) class: head
+// pairs or heads.
+__device__ __forceinline__ int sched_levels(const PrefillParams& p) {
+  return p.pair_heads ? p.n_q_tiles : (p.n_q_tiles + 1) / 2;
+}
+__device__ __forceinline__ int sched_class_items(const PrefillParams& p) { return p.pair_heads ? p.Hq / 2 : p.Hq; }
+
 __device__ __forceinline__ void build_sched(const PrefillParams& p, VarlenSched* vs) {
   for (int b = threadIdx.x; b < p.B; b += blockDim.x) {
     const int len = min(max(__ldg(p.varlen + b), 0), p.S);
-    vs->ntiles[b] = (int16_t)((len + BM - 1) / BM);
+    const int nt = (len + BM - 1) / BM;
+    vs->ntiles[b] = (int16_t)(p.pair_heads ? nt : (nt + 1) / 2);  // levels the sequence reaches
   }
   __syncthreads();
   for (int b = threadIdx.x; b < p.B; b += blockDim.x) {
@@ -195,25 +205,46 @@ __device__ __forceinline__ void build_sched(const PrefillParams& p, VarlenSched*
     }
     vs->perm[rank] = (int16_t)b;
   }
-  for (int l = threadIdx.x; l < p.n_q_tiles; l += blockDim.x) {
-    const int qt = p.n_q_tiles - 1 - l;
+  const int n_lev = sched_levels(p);
+  for (int l = threadIdx.x; l < n_lev; l += blockDim.x) {
+    const int lev = n_lev - 1 - l;
     int c = 0;
-    for (int o = 0; o < p.B; ++o) c += vs->ntiles[o] > qt ? 1 : 0;
+    for (int o = 0; o < p.B; ++o) c += vs->ntiles[o] > lev ? 1 : 0;
     vs->cnt[l] = (int16_t)c;
   }
   __syncthreads();
   if (threadIdx.x == 0) {
-    const int hp_n = p.Hq / 2;
+    const int per_cls = sched_class_items(p);
     int v = 0, z = 0;
-    for (int l = 0; l < p.n_q_tiles; ++l) {
+    for (int l = 0; l < n_lev; ++l) {
       vs->vstart[l] = v;
       vs->zstart[l] = z;
-      v += vs->cnt[l] * hp_n;
-      z += (p.B - vs->cnt[l]) * hp_n;
+      v += vs->cnt[l] * per_cls;
+      z += (p.B - vs->cnt[l]) * per_cls;
     }
-    vs->vstart[p.n_q_tiles] = v;
-    vs->zstart[p.n_q_tiles] = z;
+    vs->vstart[n_lev] = v;
+    vs->zstart[n_lev] = z;
   }
+}
+
+// Item i of the var-len order: level index l (counted from the last level),
+// batch and index inside its class.
+__device__ __forceinline__ void sched_item(const PrefillParams& p, const VarlenSched* vs, int i, int& l, int& b,
+                                           int& k) {
+  const int per_cls = sched_class_items(p);
+  const int vtot = vs->vstart[sched_levels(p)];
+  int r, first;
+  if (i < vtot) {
+    l = sched_level(vs->vstart, i);
+    r = i - vs->vstart[l];
+    first = 0;
+  } else {
+    l = sched_level(vs->zstart, i - vtot);
+    r = i - vtot - vs->zstart[l];
+    first = vs->cnt[l];
+  }
+  b = vs->perm[first + r / per_cls];
+  k = r % per_cls;
 }
 
 template <bool SCHED>
@@ -223,20 +254,9 @@ __device__ __forceinline__ Item decode_item(const PrefillParams& p, const Varlen
     const int hp_n = p.Hq / 2;
     int qt, hp;
     if constexpr (SCHED) {
-      const int vtot = vs->vstart[p.n_q_tiles];
-      int l, r, first;
-      if (i < vtot) {
-        l = sched_level(vs->vstart, i);
-        r = i - vs->vstart[l];
-        first = 0;
-      } else {
-        l = sched_level(vs->zstart, i - vtot);
-        r = i - vtot - vs->zstart[l];
-        first = vs->cnt[l];
-      }
+      int l;
+      sched_item(p, vs, i, l, it.b, hp);
       qt = p.n_q_tiles - 1 - l;
-      it.b = vs->perm[first + r / hp_n];
-      hp = r % hp_n;
     } else {
       const int per = p.B * hp_n;
       qt = p.n_q_tiles - 1 - i / per;
@@ -247,6 +267,13 @@ __device__ __forceinline__ Item decode_item(const PrefillParams& p, const Varlen
     it.h[0] = 2 * hp;
     it.h[1] = 2 * hp + 1;
     it.q0[0] = it.q0[1] = qt * BM;
+  } else if constexpr (SCHED) {
+    int l, h;
+    sched_item(p, vs, i, l, it.b, h);
+    const int qp = (p.n_q_tiles + 1) / 2 - 1 - l;
+    it.h[0] = it.h[1] = h;
+    it.q0[0] = 2 * qp * BM;
+    it.q0[1] = (2 * qp + 1) * BM;
   } else {
     const int per = p.B * p.Hq, n_qp = (p.n_q_tiles + 1) / 2;
     const int qp = n_qp - 1 - i / per, r = i % per;
@@ -937,7 +964,8 @@ static int prefill_entry(const akt_prefill_args* a, float* lse, int64_t lse_sb, 
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   // var-len work order from the lengths when the table holds the batch (any
   // other call keeps the plain order)
-  const bool sched = p.varlen && p.pair_heads && p.B <= kSchedMaxB && p.n_q_tiles <= kSchedMaxTiles;
+  const int levels = p.pair_heads ? p.n_q_tiles : (p.n_q_tiles + 1) / 2;
+  const bool sched = p.varlen && p.B <= kSchedMaxB && levels <= kSchedMaxTiles;
   if (a->dtype == AKT_FLOAT16)
     return a->head_dim == 64 ? dispatch_prefill<__half, 64>(mq, mk, mv, p, lse != nullptr, sched, st)
                              : dispatch_prefill<__half, 128>(mq, mk, mv, p, lse != nullptr, sched, st);

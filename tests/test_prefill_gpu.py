@@ -95,13 +95,15 @@ def test_prefill_varlen_shapes(causal):
 
 # The var-len kernel orders its work from the lengths (real query tiles by
 # causal cost, then the tiles past each sequence's length); these cases cover
-# zero-length and one-row sequences, ties, D=128, an odd group (one query head
-# per item, plain order) and more batches than the order table holds (plain
-# order).  Output is independent of the order, so all match the oracle.
+# zero-length and one-row sequences, ties, D=128, odd groups and plain
+# multi-head attention (one query head and two query tiles per item) and more
+# batches than the order table holds (plain order).  Output is independent of the order, so all match the oracle.
 @pytest.mark.parametrize("B,Hq,Hkv,S,D,lens", [
     (6, 8, 2, 384, 64, [0, 384, 5, 384, 250, 128]),
     (5, 8, 2, 300, 128, [300, 0, 77, 299, 1]),
     (4, 6, 2, 256, 64, [256, 0, 129, 40]),
+    (5, 4, 4, 640, 64, [640, 3, 0, 257, 600]),
+    (3, 3, 3, 300, 128, [1, 300, 130]),
     (257, 2, 1, 64, 64, None),
 ])
 def test_prefill_varlen_work_order(B, Hq, Hkv, S, D, lens):
