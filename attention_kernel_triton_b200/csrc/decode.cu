@@ -167,14 +167,36 @@ __global__ void __launch_bounds__(kDecodeThreads, (G * D > 512) ? 2 : 3) decode_
     grid_dep_wait();  // chunk offsets come from the planner kernel
     const int total = p.chunk_offset[p.B];
     if (cg >= total) return;
-    int lo = 0, hi = p.B - 1;  // largest b with chunk_offset[b] <= cg
-    while (lo < hi) {
-      int mid = (lo + hi + 1) >> 1;
-      if (p.chunk_offset[mid] <= cg) lo = mid; else hi = mid - 1;
+    if (p.B <= kDecodeThreads) {
+      // one thread per sequence, all loads in one round: the sequence whose
+      // chunk range holds cg (exactly one; empty ranges never match) publishes
+      // itself, the chunk index and its length (a binary search is a chain of
+      // dependent loads ahead of the CTA's first copy)
+      __shared__ int seq_s[3];
+      const int t = threadIdx.x;
+      if (t < p.B) {
+        const int a = p.chunk_offset[t], z = p.chunk_offset[t + 1];
+        const int len = paged_seq_len(p, t);
+        if (a <= cg && cg < z) {
+          seq_s[0] = t;
+          seq_s[1] = cg - a;
+          seq_s[2] = len;
+        }
+      }
+      __syncthreads();
+      b = seq_s[0];
+      c = seq_s[1];
+      seq_len = seq_s[2];
+    } else {
+      int lo = 0, hi = p.B - 1;  // largest b with chunk_offset[b] <= cg
+      while (lo < hi) {
+        int mid = (lo + hi + 1) >> 1;
+        if (p.chunk_offset[mid] <= cg) lo = mid; else hi = mid - 1;
+      }
+      b = lo;
+      c = cg - p.chunk_offset[b];
+      seq_len = paged_seq_len(p, b);
     }
-    b = lo;
-    c = cg - p.chunk_offset[b];
-    seq_len = paged_seq_len(p, b);
   } else {
     b = cg / p.chunks_per_seq;
     c = cg - b * p.chunks_per_seq;
