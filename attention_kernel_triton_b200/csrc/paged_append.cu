@@ -45,6 +45,9 @@ struct AppendParams {
 };
 
 constexpr int kTokensPerCta = 16;
+// 16-byte copies in flight per thread (cfg0's K/V, 67 MB: 19.9-20.0 us at 8,
+// 20.2 at 4, 21.1 at 16)
+constexpr int kPieces = 8;
 
 // Destination row (K half; V is s_kv further) of appended token `tok`, or null
 // when the page table does not place it (recorded in the status word).
@@ -87,13 +90,13 @@ __global__ void __launch_bounds__(256) append_paged_kernel(const AppendParams p)
   const int nt = rest < kTokensPerCta ? (int)rest : kTokensPerCta;
   if (threadIdx.x < nt) dst_s[threadIdx.x] = append_dst(p, t0 + threadIdx.x);
   __syncthreads();
-  // four pieces per thread per round: their loads are independent and in flight together
+  // kPieces pieces per thread per round: their loads are independent and in flight together
   const int n = nt * (int)p.div_tok.d;
-  for (int w0 = threadIdx.x; w0 < n; w0 += 4 * blockDim.x) {
-    uint4 val[4];
-    char* to[4];
+  for (int w0 = threadIdx.x; w0 < n; w0 += kPieces * blockDim.x) {
+    uint4 val[kPieces];
+    char* to[kPieces];
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
+    for (int u = 0; u < kPieces; ++u) {
       const int w = w0 + u * blockDim.x;
       to[u] = nullptr;
       if (w >= n) continue;
@@ -109,7 +112,7 @@ __global__ void __launch_bounds__(256) append_paged_kernel(const AppendParams p)
       to[u] = dst + kv * p.s_kv + h * p.s_head + c * 16;
     }
 #pragma unroll
-    for (int u = 0; u < 4; ++u)
+    for (int u = 0; u < kPieces; ++u)
       if (to[u]) *reinterpret_cast<uint4*>(to[u]) = val[u];
   }
 }
