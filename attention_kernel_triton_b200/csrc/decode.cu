@@ -397,7 +397,8 @@ struct Plan {
 
 // Tuning knobs, read once per thread: AKT_DECODE_STAGE_KB (shared-memory
 // budget of the K/V stage ring per CTA, default 64), AKT_DECODE_CHUNK_TILES
-// (upper bound on tiles per split-KV chunk, default 128) and
+// (upper bound on tiles per split-KV chunk, default 128; dense inputs count
+// 16 KB tiles, two of their 8 KB ones) and
 // AKT_DECODE_ITEMS_PER_SM (work items aimed at per SM, default 3: about one
 // wave at three CTAs per SM; large inputs hit the chunk bound instead).
 int env_int(const char* name, int dflt) {
