@@ -25,6 +25,9 @@
 #include "common.cuh"
 #include "profile.cuh"
 
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
 #include <algorithm>
 #include <cstdio>
 #include <cstdlib>
@@ -74,6 +77,7 @@ struct DecodeParams {
   float* part_o;      // [items, G_TILE, D]
   float* part_lse;    // [items, G_TILE]   (log2 domain)
   int* chunk_offset;  // [B + 1] paged only
+  int max_chunks;     // paged: chunks the workspace holds per unit (the planner clamps to it)
   int direct_out;     // every unit has one chunk: write O directly
 };
 
@@ -89,6 +93,12 @@ __device__ __forceinline__ int paged_seq_len(const DecodeParams& p, int b) {
   return (np - 1) * p.P + last;
 }
 
+// Chunk offsets are clamped to p.max_chunks, the count the workspace was sized
+// for (num_page_entries * P / chunk_tokens + B, which a well-formed indptr never
+// exceeds: its ranges are disjoint and inside the index array).  An indptr whose
+// ranges overlap can ask for more; its excess chunks are dropped and recorded as
+// kStatusBadIndptr, so neither the split-KV kernel nor the merge ever reads or
+// writes past the workspace.
 __global__ void __launch_bounds__(1024) paged_plan_kernel(DecodeParams p) {
   __shared__ int warp_sums[32];
   __shared__ int carry;
@@ -103,7 +113,8 @@ __global__ void __launch_bounds__(1024) paged_plan_kernel(DecodeParams p) {
       if (e < s || s < 0 || e > p.num_page_entries) {
         record_status(kStatusBadIndptr);
       } else {
-        n = cdiv(paged_seq_len(p, b), p.chunk_tokens);
+        // at most max_chunks + 1 per sequence, so the sums below cannot overflow
+        n = min(cdiv(paged_seq_len(p, b), p.chunk_tokens), p.max_chunks + 1);
       }
     }
     int x = n;
@@ -125,12 +136,15 @@ __global__ void __launch_bounds__(1024) paged_plan_kernel(DecodeParams p) {
     }
     __syncthreads();
     const int incl = x + (warp > 0 ? warp_sums[warp - 1] : 0);  // inclusive, within this block
-    if (b < p.B) p.chunk_offset[b] = carry + incl - n;
+    if (b < p.B) p.chunk_offset[b] = min(carry + incl - n, p.max_chunks);
     __syncthreads();
-    if (threadIdx.x == 1023) carry += incl;  // n == 0 past the end, so this is the block total
+    if (threadIdx.x == 1023) carry = min(carry + incl, p.max_chunks + 1);  // block total (n == 0 past the end)
     __syncthreads();
   }
-  if (threadIdx.x == 0) p.chunk_offset[p.B] = carry;
+  if (threadIdx.x == 0) {
+    if (carry > p.max_chunks) record_status(kStatusBadIndptr);
+    p.chunk_offset[p.B] = min(carry, p.max_chunks);
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -685,6 +699,7 @@ int akt_decode_paged(const akt_decode_paged_args* a, void* ws, size_t ws_bytes, 
   p.tile_tokens = pl.tile_tokens; p.chunk_tokens = pl.chunk_tokens; p.chunks_per_seq = 0;
   p.num_stages = pl.num_stages; p.scale_log2 = a->softmax_scale * kLog2e;
   p.direct_out = 0;
+  p.max_chunks = (int)std::min<int64_t>(pl.items / p.units, INT32_MAX - 1);
   p.part_o = reinterpret_cast<float*>(ws);
   p.part_lse = reinterpret_cast<float*>(static_cast<char*>(ws) + pl.off_lse);
   p.chunk_offset = reinterpret_cast<int*>(static_cast<char*>(ws) + pl.off_chunk);
@@ -719,21 +734,45 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratch
 constexpr int kMaxDevices = 64;
 std::mutex g_noalloc_mu;
 void* g_noalloc_ptr[kMaxDevices] = {};
+CUcontext g_noalloc_ctx[kMaxDevices] = {};
 
-// Device address of the scratch array on the current device, looked up once
-// per device (the first call on a device does this set-up).
+// The driver's current context, through the runtime's entry-point query (the
+// library links only the runtime).  Null if the query is unavailable.
+CUcontext current_context() {
+  static PFN_cuCtxGetCurrent_v4000 fn = [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    return (cudaGetDriverEntryPoint("cuCtxGetCurrent", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+               ? reinterpret_cast<PFN_cuCtxGetCurrent_v4000>(f)
+               : nullptr;
+  }();
+  CUcontext c = nullptr;
+  if (fn) fn(&c);
+  return c;
+}
+
+// Device address of the scratch array on the current device.  It is looked up
+// on the first call on a device, and again whenever the context current at the
+// call differs from the one it was looked up under (a caller on its own
+// driver-API context gets that context's copy of the module).  A device reset
+// (cudaDeviceReset) unloads the module; the address cached before it is not
+// detected as stale, so a process that resets a device must not call this
+// entry point on that device afterwards.
 int noalloc_scratch(void** out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return set_error(AKT_ERR_CUDA, std::string("cudaGetDevice: ") + cudaGetErrorString(e));
   if (dev < 0 || dev >= kMaxDevices) return set_error(AKT_ERR_INVALID, "device ordinal out of range");
+  const CUcontext ctx = current_context();
   std::lock_guard<std::mutex> lock(g_noalloc_mu);
-  if (!g_noalloc_ptr[dev]) {
+  if (!g_noalloc_ptr[dev] || g_noalloc_ctx[dev] != ctx) {
     void* ptr = nullptr;
     e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
     if (e != cudaSuccess || !ptr)
       return set_error(AKT_ERR_CUDA, std::string("cudaGetSymbolAddress(scratch): ") + cudaGetErrorString(e));
     g_noalloc_ptr[dev] = ptr;
+    g_noalloc_ctx[dev] = current_context();  // the runtime call above may have made the primary context current
   }
   *out = g_noalloc_ptr[dev];
   return AKT_OK;
@@ -791,6 +830,7 @@ extern "C" int akt_decode_paged_noalloc(const akt_decode_paged_args* a, void* st
   p.tile_tokens = pl.tile_tokens; p.chunk_tokens = pl.chunk_tokens; p.chunks_per_seq = 0;
   p.num_stages = pl.num_stages; p.scale_log2 = a->softmax_scale * kLog2e;
   p.direct_out = 0;
+  p.max_chunks = (int)std::min<int64_t>(pl.items / p.units, INT32_MAX - 1);
   p.part_o = reinterpret_cast<float*>(ws);
   p.part_lse = reinterpret_cast<float*>(static_cast<char*>(ws) + pl.off_lse);
   p.chunk_offset = reinterpret_cast<int*>(static_cast<char*>(ws) + pl.off_chunk);

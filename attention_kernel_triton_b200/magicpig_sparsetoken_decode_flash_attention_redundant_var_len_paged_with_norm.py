@@ -28,14 +28,14 @@ def magicpig_sparsetoken_flash_attention_decode_paged(q, paged_kv_cache, kv_page
 
 
 def magicpig_sparsetoken_flash_attention_decode_paged_csr(q, paged_kv_cache, kv_page_indptr, kv_page_indices,
-                                                          sparse_inds, sparse_ptr, K, L, max_nnz=None):
+                                                          sparse_inds, sparse_ptr, K, L, max_nnz):
     """CSR-list variant: head ``h`` of batch ``b`` keeps
     ``sparse_inds[sparse_ptr[b*Hq + h] : sparse_ptr[b*Hq + h + 1]]`` (the ``inds`` + ``ptr``
-    format of ``sparse_decode_flash_attention.py:13-15``).  -> O [B, Hq, D]."""
+    format of ``sparse_decode_flash_attention.py:13-15``).  ``max_nnz`` (required) bounds the
+    row lengths and sizes the scratch; no device read.  -> O [B, Hq, D]."""
     B, H_q, _, D = q.shape
     assert sparse_ptr.numel() == B * H_q + 1, "sparse_ptr must hold B * Hq + 1 offsets"
-    if max_nnz is None:
-        max_nnz = csr_max_nnz(sparse_ptr)
+    max_nnz = csr_max_nnz(max_nnz)
     output = torch.empty((B, H_q, D), device=q.device, dtype=q.dtype)
     return sparse_paged_call("akt_magicpig_paged_csr", output, q, paged_kv_cache, kv_page_indptr, kv_page_indices,
                              sparse_inds.reshape(-1), None, 1.0 / math.sqrt(D), K=K, L=L,

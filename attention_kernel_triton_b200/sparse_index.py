@@ -84,7 +84,9 @@ def sparse_csr_from_lists(sparse_ind: torch.Tensor, sparse_nnz: torch.Tensor):
     """Padded lists ``(sparse_ind [B, H, L_max], sparse_nnz [B, H(, 1)])`` -> CSR
     ``(inds [sum nnz] int32, ptr [B*H + 1] int32)``: row ``b*H + h`` is
     ``inds[ptr[b*H + h] : ptr[b*H + h + 1]]``, the first ``nnz`` entries of that list
-    (``nnz`` clamped to ``[0, L_max]``).  Device-side torch ops, no host copy."""
+    (``nnz`` clamped to ``[0, L_max]``).  Device-side torch ops; the boolean selection
+    sizes its output, which costs one host synchronisation (a list-building step, not a
+    decode launch)."""
     dev = _lib.require_cuda(sparse_ind, sparse_nnz)
     B, H, L_max = sparse_ind.shape
     n = sparse_nnz.reshape(B * H).to(torch.int64).clamp(0, L_max)

@@ -101,15 +101,17 @@ def sparsetoken_flash_attention_decode(q, K, V, sparse_ind, sparse_nnz, softmax_
 
 
 def sparsetoken_flash_attention_decode_csr(q, K, V, sparse_inds, sparse_ptr, softmax_scale, GQA_group_size,
-                                           max_nnz=None):
+                                           max_nnz):
     """CSR-list variant (the ``inds`` + ``ptr`` format of the reference's notes,
     ``sparse_decode_flash_attention.py:13-15``): head ``h`` of batch ``b`` keeps
     ``sparse_inds[sparse_ptr[b*Hq + h] : sparse_ptr[b*Hq + h + 1]]`` (ascending token positions).
-    ``max_nnz`` bounds the row lengths (it sizes the split-KV scratch); when omitted it is
-    read from ``sparse_ptr`` with one device-to-host copy.  -> O [B, Hq, 1, D]."""
+    ``max_nnz`` (required) bounds the row lengths and sizes the split-KV scratch, so the
+    call reads nothing back from the device; rows longer than it are cut there and the cut
+    is recorded in the device status word (code 3).  -> O [B, Hq, 1, D]."""
     B, Hq, _, D = q.shape
-    if max_nnz is None:
-        max_nnz = int((sparse_ptr[1:] - sparse_ptr[:-1]).max().item()) if sparse_ptr.numel() > 1 else 0
+    max_nnz = int(max_nnz)
+    if max_nnz < 0:
+        raise ValueError("max_nnz must be non-negative")
     O = torch.empty((B, Hq, 1, D), dtype=q.dtype, device=q.device)
     _lib.require_cuda(O, sparse_inds, sparse_ptr)
     assert sparse_ptr.numel() == B * Hq + 1, "sparse_ptr must hold B * Hq + 1 offsets"

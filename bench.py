@@ -10,6 +10,10 @@ pages in seeded random physical order), inputs resident in HBM.  The pool is
 Multi-GPU (torchrun, one rank per GPU): every rank decodes its own cfg3 batch
 (seed + rank): weak scaling, no data-path collective.  ``value`` is the
 algorithmic bytes of all ranks divided by the max-over-ranks device time.
+``strong_scaling`` splits ONE cfg3 / cfg0 / cfg1 workload over the ranks by kv
+head (no communication) and gives its throughput and efficiency at this N;
+``parity`` checks sampled outputs of every timed run against the CPU oracle
+(max over ranks), outside the timed regions.
 
 ``--impl reference`` times the reference's naive paged decode (the CPU oracle's
 restatement of ``naive_paged_attention``, fp32 torch on all host cores) on a
@@ -167,6 +171,159 @@ def time_kernels(fn, iters, dev, flush=None):
             fn()
         torch.cuda.synchronize(dev)
     return prof.total_ms / max(prof.launches, 1)
+
+
+# ----------------------------------------------------------------------------
+# parity of the timed runs against the CPU oracle (outside every timed region)
+# ----------------------------------------------------------------------------
+TOL = 2e-3
+
+
+def _paged_sample(c, batches, heads=None):
+    """The sampled sequences of a paged case as a small CPU case (their pages only),
+    for the oracle: ``(q, cache, indptr, indices, last)``, kv heads ``heads`` of the
+    pool when given."""
+    ip = c.indptr.cpu().tolist()
+    idx = c.indices.cpu()
+    pages, counts = [], []
+    for b in batches:
+        pages.append(idx[ip[b]:ip[b + 1]])
+        counts.append(ip[b + 1] - ip[b])
+    sel = torch.cat(pages).to(c.cache.device, torch.int64)
+    cache = c.cache.index_select(0, sel)
+    if heads is not None:
+        cache = cache[:, :, heads[0]:heads[1]]
+    indptr = torch.tensor([0] + torch.tensor(counts).cumsum(0).tolist(), dtype=torch.int32)
+    indices = torch.arange(sel.numel(), dtype=torch.int32)
+    q = c.q[list(batches)].cpu()
+    last = c.last_page_len[list(batches)].cpu()
+    return q, cache.cpu(), indptr, indices, last
+
+
+def paged_parity(out, c, batches, kv_heads=None, group=None):
+    """Max-abs error of ``out`` (the decode of case ``c``, or of kv heads ``kv_heads``
+    of it) against the oracle on the sampled sequences; NaN counts as infinite."""
+    from oracle import naive as N  # checker only, outside the timed regions
+    q, cache, indptr, indices, last = _paged_sample(c, batches, kv_heads)
+    if kv_heads is not None:
+        q = q[:, kv_heads[0] * group:kv_heads[1] * group]
+    ref = N.naive_paged_attention(q, cache, indptr, indices, last)
+    got = out[list(batches)].float().cpu()
+    if torch.isnan(got).any():
+        return float("inf")
+    return float((got - ref).abs().max())
+
+
+def prefill_parity(O, f, samples, q_off=0):
+    """Max-abs error of the prefill output ``O`` (query heads ``q_off ..`` of case ``f``)
+    against the oracle on sampled (batch, local query head) pairs, valid rows only."""
+    from oracle import naive as N  # checker only
+    err = 0.0
+    for b, hl in samples:
+        h = q_off + hl
+        kvh = h // f.group
+        ref = N.prefill_reference(f.Q[b:b + 1, h:h + 1].cpu(), f.K[b:b + 1, kvh:kvh + 1].cpu(),
+                                  f.V[b:b + 1, kvh:kvh + 1].cpu(), True, f.softmax_scale, 1)
+        n = int(f.varlen[b]) if f.varlen is not None else f.Q.shape[2]
+        got = O[b:b + 1, hl:hl + 1, :n].float().cpu()
+        if torch.isnan(O[b:b + 1, hl:hl + 1]).any():
+            return float("inf")
+        err = max(err, float((got - ref[:, :, :n]).abs().max()))
+    return err
+
+
+def _max_over_ranks(pg, dev, values):
+    t = torch.tensor(values, dtype=torch.float64, device=dev)
+    if pg is not None:
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+    return [float(x) for x in t.tolist()]
+
+
+def _timed(fn, steps, dev, pg, flush=None):
+    """Mean device ms per call of ``fn`` over ``steps`` calls, max over ranks (barrier
+    and synchronize on both sides; ``flush`` is overwritten before each call)."""
+    for _ in range(3):
+        fn()
+    if pg is not None:
+        pg.barrier()
+    torch.cuda.synchronize(dev)
+    if flush is None:
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize(dev)
+        ms = e0.elapsed_time(e1) / steps
+    else:
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+        for a, b in ev:
+            flush.zero_()
+            a.record()
+            fn()
+            b.record()
+        torch.cuda.synchronize(dev)
+        ms = sum(a.elapsed_time(b) for a, b in ev) / steps
+    return _max_over_ranks(pg, dev, [ms])[0]
+
+
+def strong_scaling_measurements(dev, pg, world, rank, steps=100):
+    """One BASELINE workload partitioned over all ranks by kv head (no communication):
+    cfg3 paged decode (8 kv heads: 8/N per GPU, each rank's pool slice built before
+    timing), cfg0 causal prefill and cfg1 var-len prefill (16 kv heads: 16/N per GPU).
+    Time is the max over ranks; ``single_gpu_ms`` is the whole workload on rank 0's GPU
+    in the same run, and ``efficiency`` = single_gpu_ms / (N * ms).  Returns
+    ``(results, parity)``; parity samples each rank's output slice against the oracle."""
+    from attention_kernel_triton_b200.decode_flash_attention_redundant_var_len_paged import decode_paged_into
+    from attention_kernel_triton_b200.distributed import KVHeadPartition, decode_paged_partitioned, prefill_partitioned
+    from attention_kernel_triton_b200.prefill_flash_attention import flash_attention_prefill
+    from attention_kernel_triton_b200.prefill_flash_attention_var_len_padding import (
+        flash_attention_prefill as flash_attention_prefill_varlen)
+    res, par = {}, {}
+
+    # cfg3 paged decode by kv head (the full case on every rank, same seed; each rank keeps its slice)
+    c = W.make_paged(seed=0, device=dev)
+    part = KVHeadPartition(8, 4, world, rank)
+    local = part.local_paged_cache(c.cache)
+    out_l = torch.empty((64, part.q1 - part.q0, 128), dtype=torch.float16, device=dev)
+    ms = _timed(lambda: decode_paged_partitioned(c.q, local, c.indptr, c.indices, c.last_page_len, part, out=out_l),
+                steps, dev, pg)
+    out_full = torch.empty((64, 32, 128), dtype=torch.float16, device=dev)
+    single = _timed(lambda: decode_paged_into(out_full, c.q, c.cache, c.indptr, c.indices, c.last_page_len),
+                    steps, dev, None) if rank == 0 else 0.0
+    single = _max_over_ranks(pg, dev, [single])[0]
+    res["cfg3_paged_decode_kv_head"] = {
+        "gbs": c.bytes / ms / 1e6, "ms": ms, "kv_heads_per_gpu": part.num_local_kv_heads,
+        "single_gpu_ms": single, "efficiency": single / (world * ms), "l2": "inputs larger than L2"}
+    longest = int(torch.argmax(c.seq_lens))
+    par["cfg3_kv_head_sampled"] = paged_parity(out_l, c, [rank % 64, longest], (part.h0, part.h1), 4)
+    del c, local, out_full
+    torch.cuda.empty_cache()
+
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    for name, varlen in (("prefill_cfg0_causal_kv_head", False), ("prefill_cfg1_varlen_kv_head", True)):
+        f = W.make_prefill(seed=1 if varlen else 0, device=dev, varlen=varlen)
+        part = KVHeadPartition(16, f.group, world, rank)
+        vl = f.varlen if varlen else None
+        holder = {}
+
+        def run_part():
+            holder["O"] = prefill_partitioned(f.Q, f.K, f.V, True, f.softmax_scale, f.group, part, varlen=vl)
+        ms = _timed(run_part, 20, dev, pg, flush)
+        if rank == 0:
+            fn = (lambda: flash_attention_prefill_varlen(f.Q, f.K, f.V, True, f.softmax_scale, f.group, f.varlen)) \
+                if varlen else (lambda: flash_attention_prefill(f.Q, f.K, f.V, True, f.softmax_scale, f.group))
+            single = _timed(fn, 20, dev, None, flush)
+        else:
+            single = 0.0
+        single = _max_over_ranks(pg, dev, [single])[0]
+        res[name] = {"tflops": f.flops / ms / 1e9, "ms": ms, "kv_heads_per_gpu": part.num_local_kv_heads,
+                     "single_gpu_ms": single, "efficiency": single / (world * ms), "l2": "flushed"}
+        par[name + "_sampled"] = prefill_parity(holder["O"], f, [(rank % 8, 0), (0, part.q1 - part.q0 - 1)],
+                                                q_off=part.q0)
+        del f, holder
+        torch.cuda.empty_cache()
+    return res, par
 
 
 def secondary_measurements(dev, iters=20, only=None):
@@ -343,7 +500,19 @@ def kv_split_measurement(dev, pg, world, rank, steps=50):
     ind, nnz = shard_sparse_lists(c.sparse_ind, c.sparse_nnz, lo, hi)
     K, V = c.K[:, :, lo:hi].contiguous(), c.V[:, :, lo:hi].contiguous()
     total_bytes = c.bytes
+    # the oracle's output on rank 0 (CPU, fp32), sent to every rank for its check
+    ref = torch.zeros((1, 32, 1, 128), dtype=torch.float32, device=dev)
+    if rank == 0:
+        from oracle import naive as N  # checker only, outside the timed regions
+        ref.copy_(N.sparsetoken_naive_decode(c.q.cpu(), c.K.cpu(), c.V.cpu(), c.sparse_ind.cpu(), c.sparse_nnz.cpu(),
+                                             1.0 / math.sqrt(128), 4))
+    if pg is not None:
+        pg.broadcast(ref, 0)
     del c
+
+    def err_of(o):
+        o = o.float()
+        return float("inf") if bool(torch.isnan(o).any()) else float((o.reshape(ref.shape) - ref).abs().max())
 
     def step():
         return sparsetoken_decode_kv_split(q, K, V, ind, nnz, scale, 4)
@@ -362,6 +531,7 @@ def kv_split_measurement(dev, pg, world, rank, steps=50):
     t = torch.tensor([e0.elapsed_time(e1) / steps], dtype=torch.float64, device=dev)
     pg.all_reduce(t, op=pg.ReduceOp.MAX)
     ms = float(t[0])
+    err_nccl = err_of(step())
     # the same split with the exchange fused into the kernels (NVLink peer stores + flags)
     from attention_kernel_triton_b200.distributed import PeerKVSplit
     x = PeerKVSplit(1, 32, 128, dev)
@@ -378,6 +548,7 @@ def kv_split_measurement(dev, pg, world, rank, steps=50):
         torch.cuda.synchronize(dev)
         tp = torch.tensor([e0.elapsed_time(e1) / steps], dtype=torch.float64, device=dev)
         pg.all_reduce(tp, op=pg.ReduceOp.MAX)
+        err_peer = err_of(x.step(q))
         # and replayed as CUDA graphs (no per-step host launches)
         x.capture()
         for _ in range(3):
@@ -391,14 +562,18 @@ def kv_split_measurement(dev, pg, world, rank, steps=50):
         torch.cuda.synchronize(dev)
         tg = torch.tensor([e0.elapsed_time(e1) / steps], dtype=torch.float64, device=dev)
         pg.all_reduce(tg, op=pg.ReduceOp.MAX)
+        err_graph = err_of(x.step_graph(q))
+        torch.cuda.synchronize(dev)
     finally:
         x.close()
     ms_graph = float(tg[0])
     ms_peer = float(tp[0])
+    errs = _max_over_ranks(pg, dev, [err_nccl, err_peer, err_graph])
+    parity = {"kv_split_128k_nccl": errs[0], "kv_split_128k_peer": errs[1], "kv_split_128k_peer_graph": errs[2]}
     return {"gbs": total_bytes / ms / 1e6, "ms": ms, "n_gpus": world, "mb": total_bytes / 1e6,
             "allgather_bytes_per_rank": 32 * (128 + 1) * 4, "steps": steps,
             "peer_exchange": {"gbs": total_bytes / ms_peer / 1e6, "ms": ms_peer},
-            "peer_exchange_graph": {"gbs": total_bytes / ms_graph / 1e6, "ms": ms_graph}}
+            "peer_exchange_graph": {"gbs": total_bytes / ms_graph / 1e6, "ms": ms_graph}}, parity
 
 
 def run_ours(args):
@@ -454,6 +629,8 @@ def run_ours(args):
     ms, kern_ms = float(t[0]), float(t[1])
     ms_step = ms / args.steps
     value = world * nbytes / (ms_step * 1e-3) / 1e9
+    # parity of the timed output (the last step's) on two sampled sequences of this rank's batch
+    parity = {"cfg3_weak_sampled": paged_parity(out, c, [rank % args.batch, int(torch.argmax(c.seq_lens))])}
 
     # e2e through the public API: per step, the step's inputs (q and the page
     # table) come from pinned host memory and the output goes back to host.
@@ -510,28 +687,38 @@ def run_ours(args):
     barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(compute)
+    h0 = time.perf_counter()
     run_steps(e2e_steps, start=e0)
     e1.record(compute)
+    host_ms = (time.perf_counter() - h0) * 1e3 / e2e_steps  # host time to issue one step (no waits inside)
     torch.cuda.synchronize(dev)
     e2e_ms = e0.elapsed_time(e1) / e2e_steps
-    t = torch.tensor([e2e_ms], dtype=torch.float64, device=dev)
-    if pg is not None:
-        pg.all_reduce(t, op=pg.ReduceOp.MAX)
-    e2e_ms = float(t[0])
+    e2e_ms, host_ms = _max_over_ranks(pg, dev, [e2e_ms, host_ms])
     e2e_val = world * nbytes / (e2e_ms * 1e-3) / 1e9
 
     peak, peak_kind = measured_peaks()
     achieved = nbytes / (kern_ms * 1e-3) / 1e9
     result = None
     secondary = None
+    del c
+    torch.cuda.empty_cache()
+    strong = None
+    if not args.no_strong:
+        strong, p_strong = strong_scaling_measurements(dev, pg, world, rank)
+        parity.update(p_strong)
     if world == 1 and not args.no_secondary:
-        del c
-        torch.cuda.empty_cache()
         secondary = secondary_measurements(dev)
     elif world > 1 and not args.no_secondary:
-        del c
-        torch.cuda.empty_cache()
-        secondary = {"kv_split_128k": kv_split_measurement(dev, pg, world, rank)}
+        split, p_split = kv_split_measurement(dev, pg, world, rank)
+        secondary = {"kv_split_128k": split}
+        parity.update(p_split)
+    names = sorted(parity)
+    vals = _max_over_ranks(pg, dev, [parity[k] for k in names])
+    checks = dict(zip(names, vals))
+    parity = {"tol": TOL, "max_abs": max(vals), "nan": any(v == float("inf") for v in vals),
+              "pass": all(v <= TOL for v in vals), "checks": checks,
+              "against": "CPU oracle (fp32 restatement of the reference's naive functions), sampled outputs of "
+                         "the timed runs, max over ranks"}
     if rank == 0:
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
@@ -561,10 +748,13 @@ def run_ours(args):
                          "traffic_over_algorithmic": CFG3_TRAFFIC_BYTES / nbytes if args.batch == 64 else None},
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_val, "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "ms_per_step": e2e_ms},
+                    "ms_per_step": e2e_ms, "host_issue_ms_per_step": host_ms},
+            "parity": parity,
             "gpu_launches": 3 * args.steps,
             "clocks": clk,
         }
+        if strong is not None:
+            result["strong_scaling"] = strong
         if secondary is not None:
             result["secondary"] = secondary
         print(json.dumps(result), flush=True)
@@ -585,6 +775,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-secondary", action="store_true",
                     help="skip the other configurations (prefill, dense decode, sparse)")
+    ap.add_argument("--no-strong", action="store_true",
+                    help="skip the strong-scaling partitions of one cfg3 / cfg0 / cfg1 workload")
     ap.add_argument("--only", default=None,
                     help="run just one secondary configuration by name and print it (profiler captures)")
     args = ap.parse_args()

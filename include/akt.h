@@ -161,9 +161,13 @@ int akt_decode_paged(const akt_decode_paged_args* args, void* workspace, size_t 
  * not fit returns AKT_ERR_WORKSPACE with the size it needed.  The first call
  * on a device looks up that array's device address (set-up, once per device,
  * with the target device current); make that first call before any stream
- * capture.  All calls share the array and it keeps the last call's contents
- * (nothing in it needs to start at zero): calls that overlap on the GPU, on
- * any streams, race and must not be issued. */
+ * capture.  The address is looked up again when the context current at a
+ * call differs from the one it was found under (a driver-API caller with its
+ * own context); a device reset (cudaDeviceReset) is not detected, so a
+ * process must not call this entry point on a device after resetting it.
+ * All calls share the array and it keeps the last call's contents (nothing in
+ * it needs to start at zero): calls that overlap on the GPU, on any streams,
+ * race and must not be issued. */
 int akt_decode_paged_noalloc(const akt_decode_paged_args* args, void* stream);
 
 /* ------------------------------------------------------------------------ */

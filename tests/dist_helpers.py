@@ -30,3 +30,32 @@ def oracle_merge(out, recv, rows, D):
     o = recv[:, : rows * D].view(n, rows, D)
     lse = recv[:, rows * D:]
     out.view(rows, D).copy_(N.lse_merge_reference(o, lse).to(out.dtype))
+
+
+def oracle_paged_partial(buf, rows, D, q, shard, ind, nnz, K=None, L=None):
+    """CPU stand-in for the paged partial: softmax over the kept tokens the shard's
+    page table holds (MagicPIG scores when ``K``/``L`` are given)."""
+    B, Hq = q.shape[0], q.shape[1]
+    o = buf[: rows * D].view(B, Hq, D)
+    lse = buf[rows * D:].view(B, Hq)
+    cache = shard.cache.float()
+    P = cache.shape[3]
+    G = Hq // cache.shape[2]
+    qf = q.float()
+    for b in range(B):
+        for h in range(Hq):
+            n = int(nnz[b, h])
+            if n <= 0:
+                o[b, h] = 0
+                lse[b, h] = -math.inf
+                continue
+            toks = ind[b, h, :n].long()
+            phys = shard.indices[int(shard.indptr[b]) + toks // P].long()
+            k = cache[phys, 0, h // G, toks % P]
+            v = cache[phys, 1, h // G, toks % P]
+            if K is None:
+                s = (k @ qf[b, h, 0]) / math.sqrt(D)
+            else:
+                s = N.magicpig_logits(qf[b, h, 0], k, float(K[b, h]), float(L[b, h]), D)
+            lse[b, h] = torch.logsumexp(s, 0)
+            o[b, h] = torch.softmax(s, 0) @ v

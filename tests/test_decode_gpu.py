@@ -203,6 +203,36 @@ def test_paged_decode_malformed_indptr_is_reported():
     assert not torch.isnan(O).any()
 
 
+def test_paged_decode_overlapping_indptr_stays_inside_the_workspace():
+    # indptr [0, n, 0, n]: sequence 1 runs backwards (malformed) and sequences 0 and 2 both
+    # cover all n pages, so together they ask for about twice the chunks the workspace is
+    # sized for (num_page_entries * P / chunk + B).  The planner drops the excess and records
+    # the malformed indptr; nothing past the workspace is read (a NaN-filled guard follows it).
+    import ctypes
+
+    from attention_kernel_triton_b200.decode_flash_attention_redundant_var_len_paged import _paged_args
+    one = W.make_paged(B=1, Hq=32, Hkv=8, D=128, page_size=16, lens=[16000], seed=12)
+    n = one.indices.numel()
+    q = torch.randn((3, 32, 1, 128), generator=torch.Generator().manual_seed(5)).half()
+    indptr = torch.tensor([0, n, 0, n], dtype=torch.int32)
+    last = torch.tensor([16, 16, 16], dtype=torch.int32)
+    dq, dcache, dip, didx, dlast = cuda(q), cuda(one.cache), cuda(indptr), cuda(one.indices), cuda(last)
+    out = torch.empty((3, 32, 128), dtype=torch.float16, device=DEV)
+    a = _paged_args(dq, dcache, dip, didx, dlast, out, 1.0 / math.sqrt(128))
+    L = _lib.lib()
+    need = L.akt_decode_paged_workspace_size(ctypes.byref(a))
+    ws = torch.full((2 * need // 4 + 64,), float("nan"), dtype=torch.float32, device=DEV)
+    _lib.check(L.akt_decode_paged(ctypes.byref(a), ws.data_ptr(), need, _lib.stream_ptr(out.device)))
+    torch.cuda.synchronize()
+    assert _lib.device_status(0, clear=True) == 4
+    assert not torch.isnan(out).any()
+    assert torch.isnan(ws[(need + 3) // 4:]).all()  # the guard past the workspace is untouched
+    # sequence 0 comes first in the chunk order and keeps every chunk: exact
+    ref0 = N.naive_paged_attention(q[:1].float(), one.cache.float(), one.indptr, one.indices, one.last_page_len)
+    check_close(out[:1], ref0)
+    assert torch.all(out[1] == 0)
+
+
 # ---------------------------------------------------------------- cfg3 (B=64, lens U[512, 32768]), full size
 @pytest.fixture(scope="module")
 def cfg3():

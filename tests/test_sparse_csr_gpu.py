@@ -49,7 +49,8 @@ def test_dense_csr_matches_padded_and_golden():
     q, K, V, ind, nnz = cuda(f["q"], f["K"], f["V"], f["sparse_ind"], f["sparse_nnz"])
     inds, ptr = sparse_csr_from_lists(ind, nnz)
     O_pad = sparsetoken_flash_attention_decode(q, K, V, ind, nnz, f["softmax_scale"], f["group"])
-    O_csr = sparsetoken_flash_attention_decode_csr(q, K, V, inds, ptr, f["softmax_scale"], f["group"])
+    O_csr = sparsetoken_flash_attention_decode_csr(q, K, V, inds, ptr, f["softmax_scale"], f["group"],
+                                                   max_nnz=ind.shape[2])
     assert torch.equal(O_csr, O_pad)
     assert (O_csr.float().cpu() - f["O"]).abs().max().item() <= TOL
     assert _lib.device_status(0) == 0
@@ -71,7 +72,7 @@ def test_paged_csr_matches_padded_and_golden(name):
                                                f["sparse_nnz"])
     inds, ptr = sparse_csr_from_lists(ind, nnz)
     O_pad = sparsetoken_flash_attention_decode_paged(q, cache, indptr, indices, ind, nnz)
-    O_csr = sparsetoken_flash_attention_decode_paged_csr(q, cache, indptr, indices, inds, ptr)
+    O_csr = sparsetoken_flash_attention_decode_paged_csr(q, cache, indptr, indices, inds, ptr, max_nnz=ind.shape[2])
     assert torch.equal(O_csr, O_pad)
     assert (O_csr.float().cpu() - f["O"]).abs().max().item() <= TOL
 
@@ -82,7 +83,8 @@ def test_magicpig_csr_matches_padded_and_golden():
                                                        f["sparse_ind"], f["sparse_nnz"], f["K"], f["L"])
     inds, ptr = sparse_csr_from_lists(ind, nnz)
     O_pad = magicpig_sparsetoken_flash_attention_decode_paged(q, cache, indptr, indices, ind, nnz, Kp, Lp)
-    O_csr = magicpig_sparsetoken_flash_attention_decode_paged_csr(q, cache, indptr, indices, inds, ptr, Kp, Lp)
+    O_csr = magicpig_sparsetoken_flash_attention_decode_paged_csr(q, cache, indptr, indices, inds, ptr, Kp, Lp,
+                                                                  max_nnz=ind.shape[2])
     assert torch.equal(O_csr, O_pad)
     assert (O_csr.float().cpu() - f["O"]).abs().max().item() <= TOL
 
@@ -95,12 +97,22 @@ def test_csr_ragged_rows_empty_rows_and_no_padding():
     nnz[1, 5] = 1
     inds, ptr = sparse_csr_from_lists(c.sparse_ind, nnz)
     assert inds.numel() == int(nnz.clamp(min=0).sum())
-    O = sparsetoken_flash_attention_decode_csr(c.q, c.K, c.V, inds, ptr, c.softmax_scale, c.group)
+    O = sparsetoken_flash_attention_decode_csr(c.q, c.K, c.V, inds, ptr, c.softmax_scale, c.group,
+                                               max_nnz=c.sparse_ind.shape[2])
     assert torch.all(O[0, 3] == 0)
     ref = N.sparsetoken_naive_decode(c.q, c.K, c.V, c.sparse_ind, nnz, c.softmax_scale, c.group)
     mask = torch.ones(2, 8, dtype=torch.bool)
     mask[0, 3] = False  # the oracle reads an empty list as the reference does (index -1); we give zeros
     assert (O.float().cpu()[mask] - ref[mask]).abs().max().item() <= TOL
+
+
+def test_csr_max_nnz_is_required():
+    c = W.make_sparse_dense(B=1, Hq=4, Hkv=1, L=500, D=128, keep_p=0.05, seed=79, device=DEV)
+    inds, ptr = sparse_csr_from_lists(c.sparse_ind, c.sparse_nnz)
+    with pytest.raises(TypeError):
+        sparsetoken_flash_attention_decode_csr(c.q, c.K, c.V, inds, ptr, c.softmax_scale, c.group)
+    with pytest.raises(ValueError):
+        sparsetoken_flash_attention_decode_csr(c.q, c.K, c.V, inds, ptr, c.softmax_scale, c.group, max_nnz=-1)
 
 
 def test_csr_malformed_offsets_and_overlong_rows_are_recorded():
@@ -112,7 +124,8 @@ def test_csr_malformed_offsets_and_overlong_rows_are_recorded():
                                                max_nnz=c.sparse_ind.shape[2])
     assert _lib.device_status(0, clear=True) == 4
     assert torch.all(O[0, 1] == 0)
-    good = sparsetoken_flash_attention_decode_csr(c.q, c.K, c.V, inds, ptr, c.softmax_scale, c.group)
+    good = sparsetoken_flash_attention_decode_csr(c.q, c.K, c.V, inds, ptr, c.softmax_scale, c.group,
+                                                  max_nnz=c.sparse_ind.shape[2])
     assert torch.equal(O[0, 0], good[0, 0])
     # a bound shorter than the rows: rows are cut there and the cut is recorded
     sparsetoken_flash_attention_decode_csr(c.q, c.K, c.V, inds, ptr, c.softmax_scale, c.group, max_nnz=5)

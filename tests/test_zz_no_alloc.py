@@ -56,6 +56,29 @@ def test_noalloc_matches_workspace_entry_point_on_two_calls(shape):
     assert _lib.device_status(0) == 0
 
 
+def test_noalloc_lengthens_chunks_when_the_default_split_does_not_fit():
+    # 16 sequences of ~140K tokens (4.6 GB pool): the default split's partials need more
+    # than the 16 MiB the library holds, so the entry point plans longer chunks until they
+    # fit; the output must still match the workspace entry point, on two calls in a row
+    torch.cuda.set_device(0)
+    _lib.device_status(0, clear=True)
+    c = W.make_paged(B=16, Hq=64, Hkv=8, D=64, page_size=16, min_len=130000, max_len=150000, seed=79,
+                     device=DEV)
+    B, Hq, _, D = c.q.shape
+    scale = 1.0 / D ** 0.5
+    ref = torch.empty((B, Hq, D), dtype=c.q.dtype, device=DEV)
+    a = _paged_args(c.q, c.cache, c.indptr, c.indices, c.last_page_len, ref, scale)
+    assert _lib.lib().akt_decode_paged_workspace_size(ctypes.byref(a)) > (16 << 20)
+    decode_paged_into(ref, c.q, c.cache, c.indptr, c.indices, c.last_page_len, scale)
+    for _ in range(2):
+        out = torch.full((B, Hq, D), float("nan"), dtype=c.q.dtype, device=DEV)
+        _lib.check(_noalloc(out, c, scale))
+        torch.cuda.synchronize()
+        assert not torch.isnan(out).any()
+        assert (out.float() - ref.float()).abs().max().item() <= TOL
+    assert _lib.device_status(0) == 0
+
+
 def test_noalloc_rejects_calls_beyond_its_scratch():
     torch.cuda.set_device(0)
     c = W.make_paged(B=2, Hq=8, Hkv=2, D=128, page_size=16, lens=[40, 50], seed=78, device=DEV)
