@@ -39,6 +39,8 @@ namespace akt {
 
 __device__ unsigned int g_device_status = 0;
 
+
+
 // status word of the prefill kernels (prefill.cu is whole-program device code)
 cudaError_t prefill_status_read(unsigned int* v);
 cudaError_t prefill_status_clear();
@@ -323,12 +325,12 @@ __global__ void __launch_bounds__(kDecodeThreads, (G * D > 512) ? 2 : 3) decode_
   wa.stash(comb_m, comb_l, comb_o, cw, alive);
   named_bar_sync(1, kConsumerWarps * 32);
   const int ctid = threadIdx.x - 32 * kProducerWarps;
+  T* out = static_cast<T*>(p.out);
   for (int e = ctid; e < G * D; e += kConsumerWarps * 32) {
     const int h = e / D, d = e - h * D;
     float lse2;
     const float val = combine_warps<kConsumerWarps, G, D>(comb_m, comb_l, comb_o, h, d, lse2);
     if (p.direct_out) {
-      T* out = static_cast<T*>(p.out);
       out[(int64_t)b * p.o_sb + (int64_t)(head0 + h) * p.o_sh + (int64_t)d * p.o_sd] = E::from_float(val);
     } else {
       p.part_o[((int64_t)item * G + h) * D + d] = val;
@@ -339,6 +341,10 @@ __global__ void __launch_bounds__(kDecodeThreads, (G * D > 512) ? 2 : 3) decode_
 
 // ---------------------------------------------------------------------------
 // merge of split-KV partials: O = sum_j 2^{lse_j - M} O_j / sum_j 2^{lse_j - M}
+// One CTA per (sequence, unit).  Per head, one warp takes the max and the sum
+// of 2^(lse_j - M) over the chunks (lanes striding the chunks); then each
+// thread accumulates four consecutive dims of one head (one 16-byte load per
+// chunk, chunks unrolled so several loads are in flight).
 // ---------------------------------------------------------------------------
 template <typename T, int D, int G, bool PAGED>
 __global__ void __launch_bounds__(256) decode_merge_kernel(const DecodeParams p) {
@@ -356,22 +362,48 @@ __global__ void __launch_bounds__(256) decode_merge_kernel(const DecodeParams p)
   }
   const int kvh = unit / p.g_tiles;
   const int head0 = kvh * p.group + (unit - kvh * p.g_tiles) * G;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __shared__ float head_m[G], head_inv[G];
+  for (int h = warp; h < G; h += 8) {
+    float m = -INFINITY;
+    for (int cc = c0 + lane; cc < c1; cc += 32) m = fmaxf(m, p.part_lse[((int64_t)cc * p.units + unit) * G + h]);
+#pragma unroll
+    for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    float den = 0.f;
+    if (m != -INFINITY)
+      for (int cc = c0 + lane; cc < c1; cc += 32)
+        den += fast_exp2(p.part_lse[((int64_t)cc * p.units + unit) * G + h] - m);
+#pragma unroll
+    for (int o = 16; o; o >>= 1) den += __shfl_xor_sync(0xffffffffu, den, o);
+    if (lane == 0) {
+      head_m[h] = m;
+      head_inv[h] = den > 0.f ? 1.f / den : 0.f;
+    }
+  }
+  __syncthreads();
   T* out = static_cast<T*>(p.out);
-  for (int e = threadIdx.x; e < G * D; e += blockDim.x) {
+  for (int e = 4 * threadIdx.x; e < G * D; e += 4 * blockDim.x) {
     const int h = e / D, d = e - h * D;
-    float M = -INFINITY;
-    for (int cc = c0; cc < c1; ++cc) M = fmaxf(M, p.part_lse[((int64_t)cc * p.units + unit) * G + h]);
-    float den = 0.f, num = 0.f;
+    const float M = head_m[h];
+    float4 num = make_float4(0.f, 0.f, 0.f, 0.f);
     if (M != -INFINITY) {
+#pragma unroll 8
       for (int cc = c0; cc < c1; ++cc) {
         const int64_t it = (int64_t)cc * p.units + unit;
-        const float s = fast_exp2(p.part_lse[it * G + h] - M);
-        den += s;
-        num += s * p.part_o[(it * G + h) * D + d];
+        const float w = fast_exp2(p.part_lse[it * G + h] - M);
+        const float4 o = *reinterpret_cast<const float4*>(p.part_o + (it * G + h) * D + d);
+        num.x += w * o.x;
+        num.y += w * o.y;
+        num.z += w * o.z;
+        num.w += w * o.w;
       }
     }
-    const float val = den > 0.f ? num / den : 0.f;
-    out[(int64_t)b * p.o_sb + (int64_t)(head0 + h) * p.o_sh + (int64_t)d * p.o_sd] = E::from_float(val);
+    const float inv = head_inv[h];
+    T* orow = out + (int64_t)b * p.o_sb + (int64_t)(head0 + h) * p.o_sh;
+    orow[(int64_t)d * p.o_sd] = E::from_float(num.x * inv);
+    orow[(int64_t)(d + 1) * p.o_sd] = E::from_float(num.y * inv);
+    orow[(int64_t)(d + 2) * p.o_sd] = E::from_float(num.z * inv);
+    orow[(int64_t)(d + 3) * p.o_sd] = E::from_float(num.w * inv);
   }
 }
 
@@ -399,6 +431,8 @@ int sm_count() {
 
 namespace {
 
+size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
 struct Plan {
   int G_tile, tile_tokens, chunk_tokens, num_stages;
   int64_t items;  // upper bound (paged) or exact (dense)
@@ -408,6 +442,32 @@ struct Plan {
   size_t off_lse, off_chunk;
   bool direct;
 };
+
+// Item count and workspace layout of a plan whose chunk length is set:
+// partial O [items][G][D] fp32, partial log2-sum-exp [items][G] (when there
+// is more than one chunk per unit) and, paged, the chunk offsets [B + 1].  Paged item counts are the
+// bound num_page_entries * P / chunk_tokens + B chunks per unit.
+void layout_workspace(Plan& pl, bool paged, int B, int units, int D, int L, int P, int64_t num_page_entries) {
+  if (paged) {
+    const int64_t chunks = num_page_entries * (int64_t)P / pl.chunk_tokens + B;
+    pl.items = chunks * units;
+    pl.chunks_per_seq = 0;
+    pl.direct = false;
+  } else {
+    pl.chunks_per_seq = std::max(1, cdiv(L, pl.chunk_tokens));
+    pl.items = (int64_t)B * pl.chunks_per_seq * units;
+    pl.direct = pl.chunks_per_seq == 1;
+  }
+  size_t ws = 0;
+  if (!pl.direct) {
+    ws = align_up((size_t)pl.items * pl.G_tile * D * sizeof(float), 256);
+    pl.off_lse = ws;
+    ws += align_up((size_t)pl.items * pl.G_tile * sizeof(float), 256);
+  }
+  pl.off_chunk = ws;
+  if (paged) ws += align_up((size_t)(B + 1) * sizeof(int), 256);
+  pl.ws_bytes = ws;
+}
 
 // Tuning knobs, read once per thread: AKT_DECODE_STAGE_KB (shared-memory
 // budget of the K/V stage ring per CTA, default 64), AKT_DECODE_CHUNK_TILES
@@ -440,7 +500,6 @@ int largest_divisor_le(int n, int cap) {
   return 1;
 }
 
-size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
 Plan make_plan(bool paged, int B, int Hq, int Hkv, int D, int L, int P, int64_t num_page_entries,
                size_t elem_size) {
@@ -489,28 +548,10 @@ Plan make_plan(bool paged, int B, int Hq, int Hkv, int D, int L, int P, int64_t 
   const int64_t max_ct = (int64_t)env_int("AKT_DECODE_CHUNK_TILES", 128) * (paged ? 1 : dense_split);
   ct = std::max<int64_t>(1, std::min<int64_t>(max_ct, ct));
   pl.chunk_tokens = (int)(ct * pl.tile_tokens);
-  if (paged) {
-    const int64_t chunks = num_page_entries * (int64_t)P / pl.chunk_tokens + B;
-    pl.items = chunks * units;
-    pl.chunks_per_seq = 0;
-    pl.direct = false;
-  } else {
-    pl.chunks_per_seq = std::max(1, cdiv(L, pl.chunk_tokens));
-    pl.items = (int64_t)B * pl.chunks_per_seq * units;
-    pl.direct = pl.chunks_per_seq == 1;
-  }
   pl.smem = (size_t)pl.num_stages * stage_bytes +
             sizeof(float) * ((size_t)kConsumerWarps * pl.G_tile * (2 + D) + (size_t)kConsumerWarps * kSubTile * pl.G_tile) +
             sizeof(uint64_t) * 2 * pl.num_stages;
-  size_t ws = 0;
-  if (!pl.direct) {
-    ws = align_up((size_t)pl.items * pl.G_tile * D * sizeof(float), 256);
-    pl.off_lse = ws;
-    ws += align_up((size_t)pl.items * pl.G_tile * sizeof(float), 256);
-  }
-  pl.off_chunk = ws;
-  if (paged) ws += align_up((size_t)(B + 1) * sizeof(int), 256);
-  pl.ws_bytes = ws;
+  layout_workspace(pl, paged, B, units, D, L, P, num_page_entries);
   return pl;
 }
 
@@ -528,7 +569,7 @@ int launch_decode(DecodeParams p, const Plan& pl, cudaStream_t st) {
       kern<<<(unsigned)pl.items, kDecodeThreads, pl.smem, st>>>(p);
     if (e != cudaSuccess) return set_error(AKT_ERR_CUDA, std::string("decode launch: ") + cudaGetErrorString(e));
   }
-  if (!pl.direct) {
+  if (!pl.direct) {  // the merge (also zeros for a dense call over no keys or an empty sequence)
     const unsigned nb = (unsigned)p.B * p.units;
     if (nb > 0) e = launch_dependent(decode_merge_kernel<T, D, G, PAGED>, dim3(nb), dim3(256), 0, st, p);
     if (e != cudaSuccess) return set_error(AKT_ERR_CUDA, std::string("decode merge launch: ") + cudaGetErrorString(e));
@@ -798,17 +839,9 @@ extern "C" int akt_decode_paged_noalloc(const akt_decode_paged_args* a, void* st
   // Same kernels as akt_decode_paged.  When the partials of the default split
   // do not fit the fixed array, use longer chunks (fewer partials) until they do.
   const int units = a->num_kv_heads * (a->num_qo_heads / a->num_kv_heads / pl.G_tile);
-  auto scratch_bytes = [&](const Plan& q) {
-    size_t ws = align_up((size_t)q.items * q.G_tile * a->head_dim * sizeof(float), 256);
-    ws += align_up((size_t)q.items * q.G_tile * sizeof(float), 256);
-    return ws + align_up((size_t)(a->batch + 1) * sizeof(int), 256);
-  };
   while (pl.ws_bytes > kNoAllocScratchBytes && pl.chunk_tokens < (1 << 20)) {
     pl.chunk_tokens *= 2;
-    pl.items = (a->num_page_entries * (int64_t)a->page_size / pl.chunk_tokens + a->batch) * units;
-    pl.off_lse = align_up((size_t)pl.items * pl.G_tile * a->head_dim * sizeof(float), 256);
-    pl.off_chunk = pl.off_lse + align_up((size_t)pl.items * pl.G_tile * sizeof(float), 256);
-    pl.ws_bytes = scratch_bytes(pl);
+    layout_workspace(pl, true, a->batch, units, a->head_dim, 0, a->page_size, a->num_page_entries);
   }
   if (pl.ws_bytes > kNoAllocScratchBytes)
     return set_error(AKT_ERR_WORKSPACE, "decode_paged_noalloc: this call needs " + std::to_string(pl.ws_bytes) +

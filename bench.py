@@ -707,14 +707,14 @@ def run_ours(args):
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph):
         graph_outs = run_steps(GRAPH_STEPS, torch.cuda.current_stream(dev))
-    reps = max(1, -(-e2e_steps // GRAPH_STEPS))
+    graph_reps = max(1, -(-e2e_steps // GRAPH_STEPS))
     for _ in range(2):
         graph.replay()
 
     def replay_all():
-        for _ in range(reps):
+        for _ in range(graph_reps):
             graph.replay()
-    e2e_ms, host_ms = timed_e2e(replay_all, reps * GRAPH_STEPS)
+    e2e_ms, host_ms = timed_e2e(replay_all, graph_reps * GRAPH_STEPS)
     # the graph's last output equals the eager decode of the same inputs
     parity["cfg3_weak_e2e_graph_vs_eager"] = float((graph_outs[-1].float() - out.float()).abs().max())
     e2e_val = world * nbytes / (e2e_ms * 1e-3) / 1e9
@@ -775,11 +775,11 @@ def run_ours(args):
             "e2e": {"value": e2e_val, "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "ms_per_step": e2e_ms, "host_issue_ms_per_step": host_ms,
                     "method": f"public API calls and each step's copies captured in a CUDA graph of {GRAPH_STEPS} "
-                              f"steps, replayed {reps} times",
+                              f"steps, replayed {graph_reps} times",
                     "eager": {"value": e2e_eager_val, "ms_per_step": eager_ms, "host_issue_ms_per_step": eager_host_ms,
                               "method": "the same steps issued from Python every step"}},
             "parity": parity,
-            "gpu_launches": 3 * args.steps,
+            "gpu_launches": 3 * args.steps,  # planner, split-KV kernel and merge per step
             "clocks": clk,
         }
         if strong is not None:
