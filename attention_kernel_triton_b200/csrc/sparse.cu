@@ -77,6 +77,7 @@ struct SparseParams {
   // peer-store exchange (partial mode): the merge also stores each partial
   // row into slot `rank` of every device's data area and, when all its CTAs
   // are done, raises flag `rank` on every device
+  int inline_plan;  // B * units <= kSThreads: every CTA computes the unit offsets itself (no planner)
   int n_peers, rank;
   uint32_t epoch;
   float* peer_data[AKT_MAX_PEERS];
@@ -328,9 +329,48 @@ __global__ void __launch_bounds__(kSThreads) sparse_decode_kernel(const SparsePa
     fence_mbar_init();
   }
   __syncthreads();
-  grid_dep_wait();  // item offsets come from the planner kernel
   const int n_units = p.B * p.units;
-  const int total = p.unit_offset[n_units];
+  // unit offsets (items per unit = ceil(max nnz of its heads / kCP), exclusive
+  // prefix): from the planner kernel, or for a few units computed here by
+  // every CTA (one thread per unit), which takes a launch off short calls;
+  // CTA 0 then also stores them for the merge kernel
+  __shared__ int uoff_s[kSThreads + 1];
+  int total;
+  if (p.inline_plan) {
+    const int t = cta.tid;
+    int n = 0;
+    if (t < n_units) {
+      const int bb = t / p.units, un = t - bb * p.units;
+      const int kv = un / p.g_tiles;
+      const int h0 = kv * p.group + (un - kv * p.g_tiles) * G;
+      int mx = 0;
+      for (int h = 0; h < G; ++h) mx = max(mx, clamped_nnz(p, bb, h0 + h));
+      n = cdiv(mx, kCP);
+    }
+    int x = n;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, x, o);
+      if (cta.lane >= o) x += y;
+    }
+    if (cta.lane == 31) cta.idx_s[cta.warp] = x;  // warp totals (idx_s is free until the first item)
+    __syncthreads();
+    int before = 0;
+    for (int w = 0; w < cta.warp; ++w) before += cta.idx_s[w];
+    const int incl = x + before;
+    uoff_s[t] = incl - n;
+    if (t == kSThreads - 1) uoff_s[kSThreads] = incl;
+    __syncthreads();
+    if (t > n_units) uoff_s[t] = uoff_s[kSThreads];  // past the last unit: the total
+    if (t == 0) uoff_s[n_units] = uoff_s[kSThreads];
+    __syncthreads();
+    if (blockIdx.x == 0 && t <= n_units) p.unit_offset[t] = uoff_s[t];
+    total = uoff_s[n_units];
+  } else {
+    grid_dep_wait();  // item offsets come from the planner kernel
+    total = p.unit_offset[n_units];
+  }
+  const int* uoff = p.inline_plan ? uoff_s : p.unit_offset;
   for (int item = blockIdx.x; item < total; item += gridDim.x) {
     // The item's unit u: the one with unit_offset[u] <= item < unit_offset[u + 1].
     // Up to kSThreads units: one round of independent loads, one thread per
@@ -340,7 +380,7 @@ __global__ void __launch_bounds__(kSThreads) sparse_decode_kernel(const SparsePa
     // and one item per CTA (short lists) is a handful of them end to end.
     if (n_units <= kSThreads) {
       if (cta.tid < n_units) {
-        const int a = p.unit_offset[cta.tid], z = p.unit_offset[cta.tid + 1];
+        const int a = uoff[cta.tid], z = uoff[cta.tid + 1];
         if (a <= item && item < z) {
           cta.item_s[0] = cta.tid;
           cta.item_s[1] = item - a;
@@ -406,8 +446,24 @@ __global__ void __launch_bounds__(kSThreads) sparse_decode_kernel(const SparsePa
   }
 }
 
+// four floats to dst: one 16-byte store where dst is 16-byte aligned (a
+// partial row's start is not, when B * Hq is not a multiple of 4)
+__device__ __forceinline__ void store4(float* dst, float4 v) {
+  if ((reinterpret_cast<uintptr_t>(dst) & 15u) == 0) {
+    *reinterpret_cast<float4*>(dst) = v;
+  } else {
+    dst[0] = v.x;
+    dst[1] = v.y;
+    dst[2] = v.z;
+    dst[3] = v.w;
+  }
+}
+
 // merge of the per-chunk partials of every (batch, unit): chunks are the
-// contiguous items unit_offset[u] .. unit_offset[u+1)
+// contiguous items unit_offset[u] .. unit_offset[u+1).  Per head, one warp
+// takes the max and the sum of 2^(lse - max) over the chunks (lanes striding
+// the chunks); then each thread accumulates four consecutive dims of one head
+// (one 16-byte load per chunk, chunks unrolled so several loads are in flight).
 template <typename T, int D, int G>
 __global__ void __launch_bounds__(256) sparse_merge_kernel(const SparseParams p) {
   using E = Elem<T>;
@@ -417,34 +473,60 @@ __global__ void __launch_bounds__(256) sparse_merge_kernel(const SparseParams p)
   const int kvh = unit / p.g_tiles;
   const int head0 = kvh * p.group + (unit - kvh * p.g_tiles) * G;
   const int i0 = p.unit_offset[u], i1 = p.unit_offset[u + 1];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __shared__ float head_m[G], head_den[G];
+  for (int h = warp; h < G; h += 8) {
+    float m = -INFINITY;
+    for (int it = i0 + lane; it < i1; it += 32) m = fmaxf(m, p.part_lse[(int64_t)it * G + h]);
+#pragma unroll
+    for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    float den = 0.f;
+    if (m != -INFINITY)
+      for (int it = i0 + lane; it < i1; it += 32) den += fast_exp2(p.part_lse[(int64_t)it * G + h] - m);
+#pragma unroll
+    for (int o = 16; o; o >>= 1) den += __shfl_xor_sync(0xffffffffu, den, o);
+    if (lane == 0) {
+      head_m[h] = m;
+      head_den[h] = den;
+    }
+  }
+  __syncthreads();
   T* out = static_cast<T*>(p.out);
-  for (int e = threadIdx.x; e < G * D; e += blockDim.x) {
+  const int64_t rows = (int64_t)p.B * p.Hq;
+  for (int e = 4 * threadIdx.x; e < G * D; e += 4 * blockDim.x) {
     const int h = e / D, d = e - h * D;
-    float M = -INFINITY;
-    for (int it = i0; it < i1; ++it) M = fmaxf(M, p.part_lse[(int64_t)it * G + h]);
-    float den = 0.f, num = 0.f;
+    const float M = head_m[h], den = head_den[h];
+    float4 num = make_float4(0.f, 0.f, 0.f, 0.f);
     if (M != -INFINITY) {
+#pragma unroll 8
       for (int it = i0; it < i1; ++it) {
-        const float s = fast_exp2(p.part_lse[(int64_t)it * G + h] - M);
-        den += s;
-        num += s * p.part_o[((int64_t)it * G + h) * D + d];
+        const float w = fast_exp2(p.part_lse[(int64_t)it * G + h] - M);
+        const float4 o = *reinterpret_cast<const float4*>(p.part_o + ((int64_t)it * G + h) * D + d);
+        num.x += w * o.x;
+        num.y += w * o.y;
+        num.z += w * o.z;
+        num.w += w * o.w;
       }
     }
-    const float val = den > 0.f ? num / den : 0.f;
+    const float inv = den > 0.f ? 1.f / den : 0.f;
+    const float4 val = make_float4(num.x * inv, num.y * inv, num.z * inv, num.w * inv);
+    const int64_t row = (int64_t)b * p.Hq + head0 + h;
     if (p.n_peers) {
-      const int64_t row = (int64_t)b * p.Hq + head0 + h, rows = (int64_t)p.B * p.Hq;
       const float lse = den > 0.f ? (M + log2f(den)) * kLn2 : -INFINITY;
       for (int r = 0; r < p.n_peers; ++r) {
         float* slot = p.peer_data[r] + (int64_t)p.rank * (rows * D + rows);
-        slot[row * D + d] = val;
+        store4(slot + row * D + d, val);
         if (d == 0) slot[rows * D + row] = lse;
       }
     } else if (p.out_part_o) {
-      const int64_t row = (int64_t)b * p.Hq + head0 + h;
-      p.out_part_o[row * D + d] = val;
+      store4(p.out_part_o + row * D + d, val);
       if (d == 0) p.out_part_lse[row] = den > 0.f ? (M + log2f(den)) * kLn2 : -INFINITY;
     } else {
-      out[(int64_t)b * p.o_sb + (int64_t)(head0 + h) * p.o_sh + (int64_t)d * p.o_sd] = E::from_float(val);
+      T* orow = out + (int64_t)b * p.o_sb + (int64_t)(head0 + h) * p.o_sh;
+      orow[(int64_t)d * p.o_sd] = E::from_float(val.x);
+      orow[(int64_t)(d + 1) * p.o_sd] = E::from_float(val.y);
+      orow[(int64_t)(d + 2) * p.o_sd] = E::from_float(val.z);
+      orow[(int64_t)(d + 3) * p.o_sd] = E::from_float(val.w);
     }
   }
   if (p.n_peers) {
@@ -517,11 +599,17 @@ int launch_sparse(const SparseParams& p, const SparsePlan& pl, cudaStream_t st) 
     return cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, kSThreads, smem) == cudaSuccess && n > 0 ? n : 1;
   }();
   const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(pl.items, (int64_t)sm_count() * resident));
-  sparse_plan_kernel<G><<<1, 1024, 0, st>>>(p);
-  if (pl.items > 0) {
+  if (p.inline_plan && pl.items > 0) {
+    // first kernel of the call (reads the caller's inputs): launched normally
     ProfileScope prof(st);
-    e = launch_dependent(kern, dim3(grid), dim3(kSThreads), smem, st, p);
-    if (e != cudaSuccess) return set_error(AKT_ERR_CUDA, std::string("sparse launch: ") + cudaGetErrorString(e));
+    kern<<<grid, kSThreads, smem, st>>>(p);
+  } else {
+    sparse_plan_kernel<G><<<1, 1024, 0, st>>>(p);
+    if (pl.items > 0) {
+      ProfileScope prof(st);
+      e = launch_dependent(kern, dim3(grid), dim3(kSThreads), smem, st, p);
+      if (e != cudaSuccess) return set_error(AKT_ERR_CUDA, std::string("sparse launch: ") + cudaGetErrorString(e));
+    }
   }
   const unsigned nb = (unsigned)(p.B * p.units);
   if (nb > 0) e = launch_dependent(sparse_merge_kernel<T, D, G>, dim3(nb), dim3(256), 0, st, p);
@@ -575,6 +663,7 @@ void fill_common(SparseParams& p, const SparsePlan& pl, void* ws) {
   p.group = p.Hq / p.Hkv;
   p.g_tiles = p.group / pl.G_tile;
   p.units = p.Hkv * p.g_tiles;
+  p.inline_plan = (int64_t)p.B * p.units <= kSThreads && pl.items > 0 ? 1 : 0;
   p.part_o = reinterpret_cast<float*>(ws);
   p.part_lse = reinterpret_cast<float*>(static_cast<char*>(ws) + pl.off_lse);
   p.unit_offset = reinterpret_cast<int*>(static_cast<char*>(ws) + pl.off_units);

@@ -158,9 +158,12 @@ def measured_tflops():
 
 
 def time_kernels(fn, iters, dev, flush=None):
-    """Mean device time (ms) of the library's main kernel over ``iters`` calls,
-    from CUDA events the library records around that kernel on its stream.
-    ``flush`` (a buffer larger than L2) is overwritten before every call."""
+    """``(kernel_ms, call_ms)`` over ``iters`` calls: the mean device time of the
+    library's main kernel, from CUDA events the library records around that kernel
+    on its stream, and the mean device time of the whole call (every kernel it
+    launches), from events around the call.  ``flush`` (a buffer larger than L2)
+    is overwritten before every call, outside both; a device sleep ahead of each
+    call keeps the host's dispatch time out of the call's events."""
     from attention_kernel_triton_b200 import _lib
     for _ in range(3):
         fn()
@@ -171,7 +174,18 @@ def time_kernels(fn, iters, dev, flush=None):
                 flush.zero_()
             fn()
         torch.cuda.synchronize(dev)
-    return prof.total_ms / max(prof.launches, 1)
+    # whole calls, without the library's profiling events between their kernels
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(iters)]
+    for a, b in ev:
+        if flush is not None:
+            flush.zero_()
+        torch.cuda._sleep(200_000)  # ~0.1 ms
+        a.record()
+        fn()
+        b.record()
+    torch.cuda.synchronize(dev)
+    call_ms = sum(a.elapsed_time(b) for a, b in ev) / iters
+    return prof.total_ms / max(prof.launches, 1), call_ms
 
 
 # ----------------------------------------------------------------------------
@@ -347,32 +361,33 @@ def secondary_measurements(dev, iters=20, only=None):
 
     def prefill_cfg0():
         c = W.make_prefill(seed=0, device=dev)
-        ms = time_kernels(lambda: flash_attention_prefill(c.Q, c.K, c.V, True, c.softmax_scale, c.group),
+        ms, call_ms = time_kernels(lambda: flash_attention_prefill(c.Q, c.K, c.V, True, c.softmax_scale, c.group),
                           iters, dev, flush)
-        return {"tflops": c.flops / ms / 1e9, "ms": ms, "frac_of_bf16_peak": c.flops / ms / 1e9 / tf,
+        return {"tflops": c.flops / ms / 1e9, "ms": ms, "call_ms": call_ms, "frac_of_bf16_peak": c.flops / ms / 1e9 / tf,
                 "gflop": c.flops / 1e9, "l2": "flushed"}
 
     def prefill_cfg1():
         c = W.make_prefill(seed=1, device=dev, varlen=True)
-        ms = time_kernels(lambda: flash_attention_prefill_varlen(c.Q, c.K, c.V, True, c.softmax_scale, c.group,
+        ms, call_ms = time_kernels(lambda: flash_attention_prefill_varlen(c.Q, c.K, c.V, True, c.softmax_scale, c.group,
                                                                  c.varlen), iters, dev, flush)
-        return {"tflops": c.flops / ms / 1e9, "ms": ms, "frac_of_bf16_peak": c.flops / ms / 1e9 / tf,
+        return {"tflops": c.flops / ms / 1e9, "ms": ms, "call_ms": call_ms, "frac_of_bf16_peak": c.flops / ms / 1e9 / tf,
                 "gflop_valid": c.flops / 1e9, "lens": c.varlen.tolist(), "l2": "flushed"}
 
     def decode(kw, fl):
         def run():
             d = W.make_decode(seed=2, device=dev, **kw)
-            ms = time_kernels(lambda: flash_attention_decode(d.q, d.K, d.V, d.softmax_scale, d.group), iters, dev,
+            ms, call_ms = time_kernels(lambda: flash_attention_decode(d.q, d.K, d.V, d.softmax_scale, d.group), iters, dev,
                               flush if fl else None)
-            return {"gbs": d.bytes / ms / 1e6, "ms": ms, "frac_of_hbm": d.bytes / ms / 1e6 / hbm,
+            return {"gbs": d.bytes / ms / 1e6, "ms": ms, "call_ms": call_ms, "call_gbs": d.bytes / call_ms / 1e6,
+                    "frac_of_hbm": d.bytes / ms / 1e6 / hbm,
                     "mb": d.bytes / 1e6, "l2": "flushed" if fl else "inputs larger than L2"}
         return run
 
     def sparse_dense():
         sd = W.make_sparse_dense(seed=41, device=dev)
-        ms = time_kernels(lambda: sparsetoken_flash_attention_decode(sd.q, sd.K, sd.V, sd.sparse_ind, sd.sparse_nnz,
+        ms, call_ms = time_kernels(lambda: sparsetoken_flash_attention_decode(sd.q, sd.K, sd.V, sd.sparse_ind, sd.sparse_nnz,
                                                                      sd.softmax_scale, sd.group), iters, dev, flush)
-        return {"gbs": sd.bytes / ms / 1e6, "ms": ms, "mb": sd.bytes / 1e6, "l2": "flushed"}
+        return {"gbs": sd.bytes / ms / 1e6, "ms": ms, "call_ms": call_ms, "mb": sd.bytes / 1e6, "l2": "flushed"}
 
     def sparse_paged(magic):
         def run():
@@ -383,24 +398,24 @@ def secondary_measurements(dev, iters=20, only=None):
             else:
                 fn = lambda: sparsetoken_flash_attention_decode_paged(  # noqa: E731
                     sp.q, sp.cache, sp.indptr, sp.indices, sp.sparse_ind, sp.sparse_nnz)
-            ms = time_kernels(fn, iters, dev, flush)
-            return {"gbs": sp.bytes / ms / 1e6, "ms": ms, "mb": sp.bytes / 1e6, "l2": "flushed"}
+            ms, call_ms = time_kernels(fn, iters, dev, flush)
+            return {"gbs": sp.bytes / ms / 1e6, "ms": ms, "call_ms": call_ms, "mb": sp.bytes / 1e6, "l2": "flushed"}
         return run
 
     def sparse_128k():
         sd = W.make_sparse_dense(B=1, Hq=32, Hkv=8, L=131072, D=128, keep_p=0.02, seed=12, device=dev, L_max=4096)
-        ms = time_kernels(lambda: sparsetoken_flash_attention_decode(sd.q, sd.K, sd.V, sd.sparse_ind, sd.sparse_nnz,
+        ms, call_ms = time_kernels(lambda: sparsetoken_flash_attention_decode(sd.q, sd.K, sd.V, sd.sparse_ind, sd.sparse_nnz,
                                                                      sd.softmax_scale, sd.group), iters, dev, flush)
-        return {"gbs": sd.bytes / ms / 1e6, "ms": ms, "mb": sd.bytes / 1e6, "l2": "flushed"}
+        return {"gbs": sd.bytes / ms / 1e6, "ms": ms, "call_ms": call_ms, "mb": sd.bytes / 1e6, "l2": "flushed"}
 
     def sparse_128k_csr():
         from attention_kernel_triton_b200.sparse_index import sparse_csr_from_lists
         sd = W.make_sparse_dense(B=1, Hq=32, Hkv=8, L=131072, D=128, keep_p=0.02, seed=12, device=dev, L_max=4096)
         inds, ptr = sparse_csr_from_lists(sd.sparse_ind, sd.sparse_nnz)
-        ms = time_kernels(lambda: sparsetoken_flash_attention_decode_csr(sd.q, sd.K, sd.V, inds, ptr,
+        ms, call_ms = time_kernels(lambda: sparsetoken_flash_attention_decode_csr(sd.q, sd.K, sd.V, inds, ptr,
                                                                          sd.softmax_scale, sd.group, max_nnz=4096),
                           iters, dev, flush)
-        return {"gbs": sd.bytes / ms / 1e6, "ms": ms, "mb": sd.bytes / 1e6, "l2": "flushed",
+        return {"gbs": sd.bytes / ms / 1e6, "ms": ms, "call_ms": call_ms, "mb": sd.bytes / 1e6, "l2": "flushed",
                 "index_bytes_csr": (inds.numel() + ptr.numel()) * 4,
                 "index_bytes_padded": sd.sparse_ind.numel() * 4 + sd.sparse_nnz.numel() * 4}
 
@@ -412,20 +427,20 @@ def secondary_measurements(dev, iters=20, only=None):
         k = torch.randn((8 * 1024, 16, 64), generator=g, device=dev, dtype=torch.float16)
         v = torch.randn((8 * 1024, 16, 64), generator=g, device=dev, dtype=torch.float16)
         app = torch.arange(0, 8 * 1024 + 1, 1024, dtype=torch.int32, device=dev)
-        ms = time_kernels(lambda: append_paged_kv_cache(c.cache, k, v, app, c.indptr, c.indices, c.last_page_len),
+        ms, call_ms = time_kernels(lambda: append_paged_kv_cache(c.cache, k, v, app, c.indptr, c.indices, c.last_page_len),
                           iters, dev, flush)
         nbytes = 2 * 2 * k.numel() * 2  # K and V rows read and written
-        return {"gbs": nbytes / ms / 1e6, "ms": ms, "frac_of_hbm": nbytes / ms / 1e6 / hbm, "mb": nbytes / 1e6,
-                "l2": "flushed"}
+        return {"gbs": nbytes / ms / 1e6, "ms": ms, "call_ms": call_ms, "frac_of_hbm": nbytes / ms / 1e6 / hbm,
+                "mb": nbytes / 1e6, "l2": "flushed"}
 
     def mask_to_index(L, L_max):
         def run():
             from attention_kernel_triton_b200.sparse_index import sparse_index_from_mask
             g = torch.Generator(device=dev).manual_seed(43)
             mask = torch.rand((1, 32, L), generator=g, device=dev) < 0.02
-            ms = time_kernels(lambda: sparse_index_from_mask(mask, L_max), iters, dev, flush)
+            ms, call_ms = time_kernels(lambda: sparse_index_from_mask(mask, L_max), iters, dev, flush)
             nbytes = mask.numel() + 32 * L_max * 4 + 32 * 4  # mask read, lists and nnz written
-            return {"gbs": nbytes / ms / 1e6, "ms": ms, "mb": nbytes / 1e6, "l2": "flushed"}
+            return {"gbs": nbytes / ms / 1e6, "ms": ms, "call_ms": call_ms, "mb": nbytes / 1e6, "l2": "flushed"}
         return run
 
     def torch_sdpa_cfg0(backend):
@@ -461,7 +476,7 @@ def secondary_measurements(dev, iters=20, only=None):
                 b.record()
             torch.cuda.synchronize(dev)
             ms = sum(a.elapsed_time(b) for a, b in ev) / iters
-            return {"tflops": c.flops / ms / 1e9, "ms": ms, "frac_of_bf16_peak": c.flops / ms / 1e9 / tf,
+            return {"tflops": c.flops / ms / 1e9, "ms": ms, "call_ms": call_ms, "frac_of_bf16_peak": c.flops / ms / 1e9 / tf,
                     "backend": backend, "l2": "flushed", "note": "library reference for context; not this repo's kernel"}
         return run
 
