@@ -196,6 +196,8 @@ SIGNATURES = {
     "akt_sparse_dense_partial_peer": (c_int, [POINTER(SparseDenseArgs), POINTER(PeerExchange), c_void_p, c_size_t,
                                               c_void_p]),
     "akt_lse_merge_peer": (c_int, [POINTER(PeerExchange), c_int64, c_int32, c_void_p, c_int64, c_int32, c_void_p]),
+    "akt_sparse_dense_split_peer": (c_int, [POINTER(SparseDenseArgs), POINTER(PeerExchange), c_void_p, c_size_t,
+                                            c_void_p]),
     "akt_mask_to_sparse_index": (c_int, [POINTER(MaskToIndexArgs), c_void_p]),
     "akt_sparse_index_to_mask": (c_int, [POINTER(IndexToMaskArgs), c_void_p]),
 }

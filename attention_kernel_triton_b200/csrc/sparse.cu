@@ -83,7 +83,18 @@ struct SparseParams {
   float* peer_data[AKT_MAX_PEERS];
   uint32_t* peer_flags[AKT_MAX_PEERS];
   uint32_t* counter;
+  // fused final merge (akt_sparse_dense_split_peer): after publishing, every
+  // merge CTA waits for all ranks' flags on this device and merges its own
+  // rows of the data area into the typed output
+  int final_merge;
+  uint32_t* merge_counter;
 };
+
+__device__ __forceinline__ uint32_t ld_acquire_sys_u32(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
 
 __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
@@ -543,6 +554,62 @@ __global__ void __launch_bounds__(256) sparse_merge_kernel(const SparseParams p)
         *p.counter = 0u;
       }
     }
+    if (p.final_merge) {
+      // wait (bounded) until every rank's partial has landed in this device's
+      // data area; every CTA of this grid is resident (the host launches this
+      // form only for a grid that fits at once), so the last one to count
+      // itself in above is never held back by a waiting one
+      const uint32_t* flags = p.peer_flags[p.rank];
+      __shared__ int ready;
+      if (threadIdx.x == 0) {
+        int ok = 1;
+        const uint64_t t0 = globaltimer_ns();
+        for (int r = 0; r < p.n_peers && ok; ++r) {
+          uint32_t spins = 0;
+          while (ld_acquire_sys_u32(flags + r) != p.epoch) {
+            if ((++spins & 255u) == 0u && globaltimer_ns() - t0 > kWaitLimitNs) {
+              record_status(kStatusWaitTimeout);
+              ok = 0;
+              break;
+            }
+          }
+        }
+        ready = ok;
+      }
+      __syncthreads();
+      // O = sum_r e^{lse_r - M} O_r / sum_r e^{lse_r - M} for this unit's rows
+      // (L2 loads: the area is written over NVLink)
+      const float* area = p.peer_data[p.rank];
+      const int64_t part = rows * D + rows;
+      for (int e = threadIdx.x; e < G * D; e += blockDim.x) {
+        const int h = e / D, d = e - h * D;
+        const int64_t row = (int64_t)b * p.Hq + head0 + h;
+        float M = -INFINITY;
+        if (ready)
+          for (int r = 0; r < p.n_peers; ++r) M = fmaxf(M, __ldcg(area + r * part + rows * D + row));
+        float den = 0.f, num = 0.f;
+        if (M != -INFINITY) {
+          for (int r = 0; r < p.n_peers; ++r) {
+            const float w = fast_exp2((__ldcg(area + r * part + rows * D + row) - M) * kLog2e);
+            den += w;
+            num += w * __ldcg(area + r * part + row * D + d);
+          }
+        }
+        out[(int64_t)b * p.o_sb + (int64_t)(head0 + h) * p.o_sh + (int64_t)d * p.o_sd] =
+            E::from_float(den > 0.f ? num / den : 0.f);
+      }
+      // the last CTA past its wait clears this device's flags for the parity's
+      // next use (a writer reaches this parity again only after this kernel)
+      __syncthreads();
+      if (threadIdx.x == 0) {
+        const unsigned fin = atomicAdd(p.merge_counter, 1u) + 1u;
+        if (fin == gridDim.x) {
+          for (int r = 0; r < p.n_peers; ++r) p.peer_flags[p.rank][r] = 0u;
+          *p.merge_counter = 0u;
+          __threadfence();
+        }
+      }
+    }
   }
 }
 
@@ -728,6 +795,7 @@ size_t akt_sparse_dense_workspace_size(const akt_sparse_dense_args* a) {
 // descriptor of the peer-store exchange for the entry point running on this
 // thread (set only for the duration of akt_sparse_dense_partial_peer)
 static thread_local const akt_peer_exchange* g_peer = nullptr;
+static thread_local bool g_peer_final = false;
 
 static int sparse_dense_entry(const akt_sparse_dense_args* a, void* ws, size_t ws_bytes, void* stream,
                               float* o_part, float* lse_part, const int32_t* csr_ptr = nullptr,
@@ -754,7 +822,7 @@ static int sparse_dense_entry(const akt_sparse_dense_args* a, void* ws, size_t w
   p.ind = a->sparse_ind; p.ind_sb = a->ind_stride_batch; p.ind_sh = a->ind_stride_head; p.ind_sp = a->ind_stride_pos;
   p.nnz = a->sparse_nnz; p.nnz_sb = a->nnz_stride_batch; p.nnz_sh = a->nnz_stride_head;
   p.csr_ptr = csr_ptr; p.num_inds = num_inds;
-  if (g_peer) {  // akt_sparse_dense_partial_peer
+  if (g_peer) {  // akt_sparse_dense_partial_peer / akt_sparse_dense_split_peer
     p.n_peers = g_peer->world;
     p.rank = g_peer->rank;
     p.epoch = g_peer->epoch;
@@ -763,6 +831,8 @@ static int sparse_dense_entry(const akt_sparse_dense_args* a, void* ws, size_t w
       p.peer_data[r] = g_peer->peer_data[r];
       p.peer_flags[r] = g_peer->peer_flags[r];
     }
+    p.final_merge = g_peer_final ? 1 : 0;
+    p.merge_counter = g_peer->merge_counter;
   }
   p.out = a->out; p.o_sb = a->out_stride_batch; p.o_sh = a->out_stride_head; p.o_sd = a->out_stride_dim;
   p.B = a->batch; p.Hq = a->num_qo_heads; p.Hkv = a->num_kv_heads; p.L = a->seq_len; p.P = 1;
@@ -809,6 +879,29 @@ int akt_sparse_dense_partial_peer(const akt_sparse_dense_args* a, const akt_peer
   g_peer = x;
   const int rc = sparse_dense_entry(a, ws, ws_bytes, stream, nullptr, nullptr);
   g_peer = nullptr;
+  return rc;
+}
+
+int akt_sparse_dense_split_peer(const akt_sparse_dense_args* a, const akt_peer_exchange* x, void* ws,
+                                size_t ws_bytes, void* stream) {
+  if (!x || x->world < 1 || x->world > AKT_MAX_PEERS || x->rank < 0 || x->rank >= x->world || !x->counter ||
+      !x->merge_counter || x->epoch == 0)
+    return set_error(AKT_ERR_INVALID, "peer exchange: bad descriptor");
+  for (int r = 0; r < x->world; ++r)
+    if (!x->peer_data[r] || !x->peer_flags[r]) return set_error(AKT_ERR_INVALID, "peer exchange: null peer pointer");
+  if (!a || !a->out) return set_error(AKT_ERR_INVALID, "split_peer: output required");
+  // the merge grid waits on itself: it must be resident at once (one CTA per
+  // (batch, unit), 256 threads; at least four fit on every SM)
+  if (a->num_kv_heads <= 0 || a->num_qo_heads % a->num_kv_heads) return set_error(AKT_ERR_INVALID, "heads");
+  const int group = a->num_qo_heads / a->num_kv_heads;
+  const int64_t units = (int64_t)a->batch * a->num_kv_heads * (group / sparse_group_tile(group, a->head_dim));
+  if (units > (int64_t)sm_count() * 4)
+    return set_error(AKT_ERR_UNSUPPORTED, "split_peer: too many (batch, unit) pairs for one resident merge grid");
+  g_peer = x;
+  g_peer_final = true;
+  const int rc = sparse_dense_entry(a, ws, ws_bytes, stream, nullptr, nullptr);
+  g_peer = nullptr;
+  g_peer_final = false;
   return rc;
 }
 

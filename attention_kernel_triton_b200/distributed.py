@@ -351,8 +351,12 @@ class PeerKVSplit:
     same order on every rank, on the current stream.  ``close()`` (collective) unmaps
     and frees; used as a context manager, the exchange closes on exit."""
 
-    def __init__(self, B: int, Hq: int, head_dim: int, device, process_group=None):
+    def __init__(self, B: int, Hq: int, head_dim: int, device, process_group=None, fused: bool = True):
         self.pg = process_group
+        # fused: the wait for the peers and the final merge run in the publishing
+        # merge kernel (akt_sparse_dense_split_peer), two launches a step; else a
+        # separate merge kernel (akt_lse_merge_peer), three
+        self.fused = fused
         self.world = dist.get_world_size(process_group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(process_group) if dist.is_initialized() else 0
         if self.world > _lib.AKT_MAX_PEERS:
@@ -420,9 +424,13 @@ class PeerKVSplit:
         assert (B, Hq, D) == (self.B, self.Hq, self.D), "shape differs from the one this exchange was built for"
         self.epoch += 1
         x = self._descriptor(self.epoch)
+        out = torch.empty((B, Hq, 1, D), dtype=q.dtype, device=q.device)
+        if self.fused:
+            _sparse_dense_call("akt_sparse_dense_split_peer", out, q, K_local, V_local, ind_local, nnz_local,
+                               softmax_scale, GQA_group_size, peer=x)
+            return out
         _sparse_dense_call("akt_sparse_dense_partial_peer", None, q, K_local, V_local, ind_local, nnz_local,
                            softmax_scale, GQA_group_size, peer=x)
-        out = torch.empty((B, Hq, 1, D), dtype=q.dtype, device=q.device)
         with torch.cuda.device(q.device):
             _lib.check(_lib.lib().akt_lse_merge_peer(ctypes.byref(x), self.rows, D, out.data_ptr(), D,
                                                      _lib.dtype_code(out), _lib.stream_ptr(q.device)))
@@ -458,6 +466,8 @@ class PeerKVSplit:
         a.max_nnz = ind.shape[2]
         a.dtype = _lib.dtype_code(q)
         a.softmax_scale = float(softmax_scale)
+        a.out = out.data_ptr()
+        a.out_stride_batch, a.out_stride_head, a.out_stride_dim = out.stride(0), out.stride(1), out.stride(3)
         assert self.Hq // K.shape[1] == GQA_group_size
         ws = _lib.workspace(L.akt_sparse_dense_workspace_size(ctypes.byref(a)), dev)
         self._bound = {"args": a, "ws": ws, "q": q, "out": out, "keep": (K, V, ind, nnz),
@@ -476,6 +486,10 @@ class PeerKVSplit:
         b = self._bound
         L = _lib.lib()
         st = _lib.stream_ptr(self.device)
+        if self.fused:
+            _lib.check(L.akt_sparse_dense_split_peer(ctypes.byref(b["args"]), ctypes.byref(x), b["ws"].data_ptr(),
+                                                     b["ws"].numel(), st))
+            return
         _lib.check(L.akt_sparse_dense_partial_peer(ctypes.byref(b["args"]), ctypes.byref(x), b["ws"].data_ptr(),
                                                    b["ws"].numel(), st))
         _lib.check(L.akt_lse_merge_peer(ctypes.byref(x), self.rows, self.D, b["out"].data_ptr(), self.D,

@@ -506,13 +506,24 @@ def secondary_measurements(dev, iters=20, only=None):
     return out
 
 
-def kv_split_measurement(dev, pg, world, rank, steps=50):
-    """128K-token single-sequence sparse decode split along the key axis over
-    all ranks: partial on each GPU, NCCL all-gather of [O | LSE], LSE merge.
-    Every rank takes the same collective steps; time is the max over ranks."""
+def kv_split_measurement(dev, pg, world, rank, steps=50, L=131072):
+    """L-token single-sequence sparse decode (2 % kept per kv head) split along the
+    key axis over all ranks: partial on each GPU, NCCL all-gather of [O | LSE], LSE
+    merge; and the same with the exchange fused into the kernels (peer stores and
+    flags, eager and as CUDA graphs).  ``single_gpu_ms`` is the whole sequence on
+    rank 0's GPU in the same run (whole calls).  Every rank takes the same
+    collective steps; times are the max over ranks."""
     from attention_kernel_triton_b200.distributed import shard_range, shard_sparse_lists, sparsetoken_decode_kv_split
-    c = W.make_sparse_dense(B=1, Hq=32, Hkv=8, L=131072, D=128, keep_p=0.02, seed=12, device=dev, L_max=4096)
-    lo, hi = shard_range(131072, world, rank)
+    from attention_kernel_triton_b200.sparsetoken_decode_flash_attention_redundant import (
+        sparsetoken_flash_attention_decode)
+    L_max = 4096 if L == 131072 else int(L * 0.02 * 1.25) + 64
+    c = W.make_sparse_dense(B=1, Hq=32, Hkv=8, L=L, D=128, keep_p=0.02, seed=12, device=dev, L_max=L_max)
+    single = 0.0
+    if rank == 0:
+        single = _timed(lambda: sparsetoken_flash_attention_decode(c.q, c.K, c.V, c.sparse_ind, c.sparse_nnz,
+                                                                   1.0 / math.sqrt(128), 4), steps, dev, None)
+    single = _max_over_ranks(pg, dev, [single])[0]
+    lo, hi = shard_range(L, world, rank)
     ind, nnz = shard_sparse_lists(c.sparse_ind, c.sparse_nnz, lo, hi)
     K, V = c.K[:, :, lo:hi].contiguous(), c.V[:, :, lo:hi].contiguous()
     total_bytes = c.bytes
@@ -524,6 +535,7 @@ def kv_split_measurement(dev, pg, world, rank, steps=50):
                                              1.0 / math.sqrt(128), 4))
     if pg is not None:
         pg.broadcast(ref, 0)
+    q_full = c.q.clone()
     del c
 
     def err_of(o):
@@ -532,7 +544,7 @@ def kv_split_measurement(dev, pg, world, rank, steps=50):
 
     def step():
         return sparsetoken_decode_kv_split(q, K, V, ind, nnz, scale, 4)
-    q = W.make_sparse_dense(B=1, Hq=32, Hkv=8, L=16, D=128, seed=12, device=dev).q
+    q = q_full
     scale = 1.0 / math.sqrt(128)
     for _ in range(3):
         step()
@@ -586,8 +598,8 @@ def kv_split_measurement(dev, pg, world, rank, steps=50):
     ms_peer = float(tp[0])
     errs = _max_over_ranks(pg, dev, [err_nccl, err_peer, err_graph])
     parity = {"kv_split_128k_nccl": errs[0], "kv_split_128k_peer": errs[1], "kv_split_128k_peer_graph": errs[2]}
-    return {"gbs": total_bytes / ms / 1e6, "ms": ms, "n_gpus": world, "mb": total_bytes / 1e6,
-            "allgather_bytes_per_rank": 32 * (128 + 1) * 4, "steps": steps,
+    return {"seq_len": L, "gbs": total_bytes / ms / 1e6, "ms": ms, "n_gpus": world, "mb": total_bytes / 1e6,
+            "single_gpu_ms": single, "allgather_bytes_per_rank": 32 * (128 + 1) * 4, "steps": steps,
             "peer_exchange": {"gbs": total_bytes / ms_peer / 1e6, "ms": ms_peer},
             "peer_exchange_graph": {"gbs": total_bytes / ms_graph / 1e6, "ms": ms_graph}}, parity
 
@@ -752,6 +764,14 @@ def run_ours(args):
         split, p_split = kv_split_measurement(dev, pg, world, rank)
         secondary = {"kv_split_128k": split}
         parity.update(p_split)
+        # longer sequences: where the split starts to beat one GPU
+        sweep = []
+        for L in (524288, 2097152):
+            torch.cuda.empty_cache()
+            m, p_m = kv_split_measurement(dev, pg, world, rank, steps=30, L=L)
+            sweep.append(m)
+            parity.update({f"{k}_L{L}": v for k, v in p_m.items()})
+        secondary["kv_split_sweep"] = sweep
     names = sorted(parity)
     vals = _max_over_ranks(pg, dev, [parity[k] for k in names])
     checks = dict(zip(names, vals))

@@ -331,6 +331,14 @@ int akt_sparse_dense_partial_peer(const akt_sparse_dense_args* args, const akt_p
                                   size_t workspace_bytes, void* stream);
 int akt_lse_merge_peer(const akt_peer_exchange* x, int64_t rows, int32_t head_dim, void* out, int64_t out_row_stride,
                        int32_t dtype, void* stream);
+/* The two calls above in one: the sparse decode over this device's tokens,  */
+/* the publication of its partial and, in the same merge kernel, the wait    */
+/* for every rank's flag and the final merge into args->out (strides of      */
+/* args).  Two launches per step instead of three.  The merge grid (one CTA  */
+/* per (batch, unit)) waits on itself, so calls with more (batch, unit)      */
+/* pairs than four per SM return AKT_ERR_UNSUPPORTED (use the pair above).   */
+int akt_sparse_dense_split_peer(const akt_sparse_dense_args* args, const akt_peer_exchange* x, void* workspace,
+                                size_t workspace_bytes, void* stream);
 
 /* ------------------------------------------------------------------------ */
 /* paged KV cache append (write path; no reference counterpart: the         */

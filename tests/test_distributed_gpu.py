@@ -129,12 +129,14 @@ def test_kv_split_nccl_two_gpus():
     assert max(errs.values()) <= TOL, errs
 
 
-def test_peer_exchange_single_device_epochs():
+@pytest.mark.parametrize("fused", [True, False])
+def test_peer_exchange_single_device_epochs(fused):
     # world 1: the kernel publishes into its own region and the merge waits on its own
-    # flag; several epochs exercise both buffer parities and the counter reset
+    # flag; several epochs exercise both buffer parities and the counter reset.  fused:
+    # the wait and the final merge run in the publishing merge kernel
     c = W.make_sparse_dense(B=1, Hq=32, Hkv=8, L=32768, D=128, keep_p=0.02, seed=31, device=DEV)
     ref = N.sparsetoken_naive_decode(c.q, c.K, c.V, c.sparse_ind, c.sparse_nnz, c.softmax_scale, c.group)
-    x = PeerKVSplit(1, 32, 128, DEV)
+    x = PeerKVSplit(1, 32, 128, DEV, fused=fused)
     try:
         for _ in range(3):
             out = x(c.q, c.K, c.V, c.sparse_ind, c.sparse_nnz, c.softmax_scale, c.group)
