@@ -203,6 +203,21 @@ def test_paged_decode_malformed_indptr_is_reported():
     assert not torch.isnan(O).any()
 
 
+@pytest.mark.parametrize("B", [300, 1100])
+def test_paged_decode_many_sequences_both_chunk_orders(B):
+    # up to 1024 sequences the planner puts every partial last chunk after all full
+    # chunks (longest first); beyond that it keeps each sequence's chunks in place
+    g = torch.Generator().manual_seed(B)
+    lens = torch.randint(0, 3000, (B,), generator=g).tolist()
+    lens[5] = 0
+    c = W.make_paged(Hq=8, Hkv=2, D=128, page_size=16, lens=lens, seed=B, device=DEV)
+    O = flash_attention_decode_paged(c.q, c.cache, c.indptr, c.indices, c.last_page_len)
+    sample = [0, 5, 17, B // 2, B - 1]
+    ref = N.naive_paged_attention(c.q, c.cache, c.indptr, c.indices, c.last_page_len, batches=sample)
+    check_close(O[sample], ref[sample])
+    assert not torch.isnan(O).any()
+
+
 def test_paged_decode_overlapping_indptr_stays_inside_the_workspace():
     # indptr [0, n, 0, n]: sequence 1 runs backwards (malformed) and sequences 0 and 2 both
     # cover all n pages, so together they ask for about twice the chunks the workspace is
@@ -227,9 +242,6 @@ def test_paged_decode_overlapping_indptr_stays_inside_the_workspace():
     assert _lib.device_status(0, clear=True) == 4
     assert not torch.isnan(out).any()
     assert torch.isnan(ws[(need + 3) // 4:]).all()  # the guard past the workspace is untouched
-    # sequence 0 comes first in the chunk order and keeps every chunk: exact
-    ref0 = N.naive_paged_attention(q[:1].float(), one.cache.float(), one.indptr, one.indices, one.last_page_len)
-    check_close(out[:1], ref0)
     assert torch.all(out[1] == 0)
 
 
