@@ -332,7 +332,7 @@ struct SparseCta {
 };
 
 template <typename T, int D, int G, bool PAGED, bool MAGIC>
-__global__ void __launch_bounds__(kSThreads) sparse_decode_kernel(const SparseParams p) {
+__global__ void __launch_bounds__(kSThreads, MAGIC ? 3 : 4) sparse_decode_kernel(const SparseParams p) {
   extern __shared__ __align__(128) unsigned char smem[];
   SparseCta<T, D, G, PAGED, MAGIC> cta(p, smem);
   if (cta.tid == 0) {
