@@ -588,7 +588,24 @@ Plan make_plan(bool paged, int B, int Hq, int Hkv, int D, int L, int P, int64_t 
   const int ips = env_int("AKT_DECODE_ITEMS_PER_SM", 3);
   const int64_t target = (int64_t)sm_count() * ips;
   int64_t ct = (total_tiles + target - 1) / target;
-  if (!paged) {
+  if (paged) {
+    // One wave of CTAs when the chunks fit the bound: the chunk length that
+    // fills `target` slots.  Otherwise bound-length chunks, unless they make
+    // between 1.25 and 4 waves: then the last wave runs part-empty, and chunks
+    // short enough for four waves are faster (one GPU's share of cfg3 split by
+    // kv head: one head 169 -> 155 us, two heads 271 -> 261 us).  Just over one
+    // wave stays (8 cfg3-like sequences: 105 us at 120-tile chunks, 118 us
+    // with four waves: the few CTAs left at the end run faster alone).
+    const int64_t one_wave = ct;
+    const int64_t max_ct_paged = env_int("AKT_DECODE_CHUNK_TILES", 128);
+    const double waves = (double)(total_tiles / max_ct_paged + (int64_t)B * units) / (double)target;
+    if (one_wave <= max_ct_paged)
+      ct = one_wave;
+    else if (waves >= 1.25 && waves < 4.0)
+      ct = std::max<int64_t>(16, std::min<int64_t>(max_ct_paged, total_tiles / (4 * target)));
+    else
+      ct = max_ct_paged;
+  } else {
     // dense: chunks are cut per (sequence, unit), so size them from the chunks
     // each one may take (the rounding of a total-based size can add a wave)
     const int64_t seq_tiles = std::max<int64_t>(1, cdiv(L, pl.tile_tokens));
