@@ -133,18 +133,28 @@ struct WarpAttn {
   // (their V rows must be finite: zero-filled or real data).  Rows above
   // row_max are never read.  score(dot, kk, head) maps a raw dot product to
   // a log2-domain score.  pw: this warp's [16][G] float scratch.
-  template <class ScoreFn>
+  // SHORT: steps may hold fewer than 16 rows (the sparse gather's 8 rows per
+  // warp), so four-row passes wholly past ns are skipped, score included.
+  template <bool SHORT = false, class ScoreFn>
   __device__ __forceinline__ void step(const T* Ks, const T* Vs, int row0, int ns, int row_max,
                                        uint32_t valid_bits, float* pw, const ScoreFn& score) {
     float sc[kRowsPerSubTile / 4];
 #pragma unroll
     for (int pass = 0; pass < kRowsPerSubTile / 4; ++pass) {
+      if (SHORT) {
+        sc[pass] = -INFINITY;
+        if (pass * 4 >= ns) continue;  // warp-uniform
+      }
       const int r = pass * 4 + tg;
       const int row = min(row0 + r, row_max);
       float kk;
       const float dot = qk_row(Ks + (size_t)row * D, kk);
       const bool valid = r < ns && ((valid_bits >> r) & 1u);
-      sc[pass] = valid ? score(dot, kk, my_head) : -INFINITY;
+      if (SHORT) {
+        if (valid) sc[pass] = score(dot, kk, my_head);
+      } else {
+        sc[pass] = valid ? score(dot, kk, my_head) : -INFINITY;
+      }
     }
     float mt = sc[0];
 #pragma unroll

@@ -199,7 +199,8 @@ struct SparseSmem {
   static constexpr size_t comb = sizeof(float) * ((size_t)kSW * G * (2 + D) + (size_t)kSW * kRowsPerSubTile * G);
   static constexpr size_t idx = sizeof(int) * ((size_t)G * kCP + G + 4);
   static constexpr size_t flags = 64;  // kCP row-valid bytes, padded
-  static constexpr size_t bytes = kv + comb + idx + flags + 16;
+  static constexpr size_t offs = sizeof(int64_t) * kCP;  // element offset of each gathered row
+  static constexpr size_t bytes = kv + comb + idx + flags + offs + 16;
 };
 
 template <typename T, int D, int G, bool PAGED, bool MAGIC>
@@ -213,6 +214,7 @@ struct SparseCta {
   int* nnz_s;
   int* item_s;  // [0] unit, [1] chunk of the current item, [2..3] indptr[b], indptr[b + 1]
   unsigned char* ok_s;
+  int64_t* off_s;
   uint64_t* bar;
   int tid, warp, lane;
   uint32_t phase;
@@ -229,7 +231,8 @@ struct SparseCta {
     nnz_s = idx_s + G * kCP;
     item_s = nnz_s + G;
     ok_s = reinterpret_cast<unsigned char*>(item_s + 4);
-    bar = reinterpret_cast<uint64_t*>((reinterpret_cast<uintptr_t>(ok_s + 64) + 7) & ~uintptr_t(7));
+    off_s = reinterpret_cast<int64_t*>((reinterpret_cast<uintptr_t>(ok_s + 64) + 7) & ~uintptr_t(7));
+    bar = reinterpret_cast<uint64_t*>(off_s + kCP);
     tid = threadIdx.x;
     warp = tid >> 5;
     lane = tid & 31;
@@ -239,10 +242,15 @@ struct SparseCta {
 
   // Gather the K/V rows of list positions rows[0..kCP) (token ids, -1 = none)
   // into Ks/Vs.  Invalid rows are zero-filled and flagged in ok_s.
+  // The first kCP threads resolve their row's element offset (the page-table
+  // lookup for paged K/V); then every thread loads 16-byte pieces of the rows
+  // with plain streaming loads, all of a thread's loads issued before its
+  // shared-memory stores.  (One 1-D bulk copy per 512-byte row took about
+  // twice as long: 64 small copies per item through the TMA engine.)
   __device__ bool gather(const int* rows, int b, int kvh) {
-    bool ok = false;
-    int64_t off = 0;
     if (tid < kCP) {
+      bool ok = false;
+      int64_t off = 0;
       const int tok = rows[tid];
       if (tok >= 0) {
         if (PAGED) {
@@ -270,29 +278,43 @@ struct SparseCta {
         }
       }
       ok_s[tid] = ok ? 1 : 0;
+      off_s[tid] = ok ? off : -1;
     }
-    const int n_ok = __syncthreads_count(ok);
-    if (tid == 0) mbar_arrive_expect_tx(bar, (uint32_t)n_ok * 2u * D * sizeof(T));
-    // zero-fill rows that get no copy so masked rows stay finite in P.V
-    for (int e = tid; e < kCP * D / 8; e += kSThreads) {
-      const int r = e / (D / 8);
-      if (!ok_s[r]) {
-        reinterpret_cast<uint4*>(Ks)[e] = make_uint4(0, 0, 0, 0);
-        reinterpret_cast<uint4*>(Vs)[e] = make_uint4(0, 0, 0, 0);
+    __syncthreads();
+    constexpr int kPiecesPerRow = D * (int)sizeof(T) / 16;
+    constexpr int kPieces = kCP * kPiecesPerRow;  // per matrix
+    constexpr int kPerThread = kPieces / kSThreads;
+    static_assert(kPieces % kSThreads == 0, "pieces per thread");
+    constexpr int kBatch = kPerThread > 4 ? 4 : kPerThread;  // loads in flight per batch (x2: K and V)
+    const uint4* kb = static_cast<const uint4*>(p.k);
+    const uint4* vb = static_cast<const uint4*>(p.v);
+    uint4* kd = reinterpret_cast<uint4*>(Ks);
+    uint4* vd = reinterpret_cast<uint4*>(Vs);
+#pragma unroll
+    for (int i0 = 0; i0 < kPerThread; i0 += kBatch) {
+      uint4 kr[kBatch], vr[kBatch];
+#pragma unroll
+      for (int i = 0; i < kBatch; ++i) {
+        const int e = tid + (i0 + i) * kSThreads;
+        const int r = e / kPiecesPerRow, c = e - r * kPiecesPerRow;
+        const int64_t o = off_s[r];
+        if (o >= 0) {
+          kr[i] = __ldcs(kb + o / 8 + c);
+          vr[i] = __ldcs(vb + o / 8 + c);
+        } else {
+          kr[i] = make_uint4(0, 0, 0, 0);
+          vr[i] = make_uint4(0, 0, 0, 0);
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < kBatch; ++i) {
+        const int e = tid + (i0 + i) * kSThreads;
+        kd[e] = kr[i];
+        vd[e] = vr[i];
       }
     }
     __syncthreads();
-    if (ok) {
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      const T* kb = static_cast<const T*>(p.k);
-      const T* vb = static_cast<const T*>(p.v);
-      bulk_g2s(Ks + tid * D, kb + off, D * sizeof(T), bar, pol);
-      bulk_g2s(Vs + tid * D, vb + off, D * sizeof(T), bar, pol);
-    }
-    bool done = mbar_wait(bar, phase & 1u);
-    if (!done) done = mbar_wait(bar, phase & 1u);  // drain copies in flight before giving up
-    ++phase;
-    return __syncthreads_and(done) != 0;  // one decision for the whole CTA
+    return true;
   }
 
   // attention of NH heads (head0 + hoff ...) over the gathered rows; writes
@@ -314,9 +336,9 @@ struct SparseCta {
       sc.K = p.mp_k[(int64_t)b * p.par_sb + (int64_t)hq * p.par_sh];
       sc.Lp = p.mp_l[(int64_t)b * p.par_sb + (int64_t)hq * p.par_sh];
       sc.inv_sqrt_d = p.inv_sqrt_d;
-      wa.step(Ks, Vs, row0, RPW, kCP - 1, bits, pw, sc);
+      wa.template step<true>(Ks, Vs, row0, RPW, kCP - 1, bits, pw, sc);
     } else {
-      wa.step(Ks, Vs, row0, RPW, kCP - 1, bits, pw, ScaledDotScore());
+      wa.template step<true>(Ks, Vs, row0, RPW, kCP - 1, bits, pw, ScaledDotScore());
     }
     wa.stash(comb_m, comb_l, comb_o, warp, true);
     __syncthreads();
