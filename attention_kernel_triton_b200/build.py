@@ -50,7 +50,8 @@ def _needs(obj: str, deps) -> bool:
 def build(verbose: bool = False, force: bool = False) -> str:
     os.makedirs(BUILD, exist_ok=True)
     srcs = sorted(glob.glob(os.path.join(CSRC, "*.cu")))
-    headers = glob.glob(os.path.join(CSRC, "*.cuh")) + glob.glob(os.path.join(ROOT, "include", "*.h"))
+    headers = (glob.glob(os.path.join(CSRC, "*.cuh")) + glob.glob(os.path.join(CSRC, "*.h")) +
+               glob.glob(os.path.join(ROOT, "include", "*.h")))
     cc = nvcc()
     jobs = []
     objs = []

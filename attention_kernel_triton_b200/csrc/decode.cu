@@ -22,6 +22,8 @@
 //    an 8-lane reduce-scatter that leaves each lane the score of one
 //    (token, head), exp2 with the scale folded into q, P.V with fp32x2 FMAs.
 #include "attn_core.cuh"
+#include "attn_mma.cuh"
+#include "tensor_map.h"
 #include "common.cuh"
 #include "profile.cuh"
 
@@ -34,6 +36,7 @@
 #include <mutex>
 #include <cstring>
 #include <string>
+#include <type_traits>
 
 namespace akt {
 
@@ -193,37 +196,36 @@ __global__ void __launch_bounds__(1024) paged_plan_kernel(DecodeParams p) {
 // ---------------------------------------------------------------------------
 // main split-KV kernel
 // ---------------------------------------------------------------------------
-template <typename T, int D, int G, bool PAGED>
-__global__ void __launch_bounds__(kDecodeThreads, (G * D > 512) ? 2 : 3) decode_splitkv_kernel(const DecodeParams p) {
-  static_assert(D % 64 == 0 && D <= 256, "head_dim");
-  static_assert(G == 1 || G == 2 || G == 4 || G == 8, "group tile");
+// The consumer warps' combined state -> the item's partial (O normalised,
+// log2-sum-exp), or the output row when the unit has one chunk.
+template <typename T, int D, int G>
+__device__ __forceinline__ void write_item(const DecodeParams& p, int item, int b, int head0, const float* comb_m,
+                                           const float* comb_l, const float* comb_o, int ctid) {
   using E = Elem<T>;
+  T* out = static_cast<T*>(p.out);
+  for (int e = ctid; e < G * D; e += kConsumerWarps * 32) {
+    const int h = e / D, d = e - h * D;
+    float lse2;
+    const float val = combine_warps<kConsumerWarps, G, D>(comb_m, comb_l, comb_o, h, d, lse2);
+    if (p.direct_out) {
+      out[(int64_t)b * p.o_sb + (int64_t)(head0 + h) * p.o_sh + (int64_t)d * p.o_sd] = E::from_float(val);
+    } else {
+      p.part_o[((int64_t)item * G + h) * D + d] = val;
+      if (d == 0) p.part_lse[(int64_t)item * G + h] = lse2;
+    }
+  }
+}
 
-  extern __shared__ __align__(128) unsigned char smem[];
-  const int NS = p.num_stages;
-  const int TT = p.tile_tokens;
-  const int stage_elems = TT * D;
-  T* kv_s = reinterpret_cast<T*>(smem);  // [NS][2][TT][D]
-  float* comb = reinterpret_cast<float*>(smem + (size_t)NS * 2 * stage_elems * sizeof(T));
-  float* comb_m = comb;                               // [NW][G]
-  float* comb_l = comb_m + kConsumerWarps * G;        // [NW][G]
-  float* comb_o = comb_l + kConsumerWarps * G;        // [NW][G][D]
-  float* p_s = comb_o + kConsumerWarps * G * D;       // [NW][kSubTile][G]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(p_s + kConsumerWarps * kSubTile * G);
-  uint64_t* full = bars;        // [NS]
-  uint64_t* empty = bars + NS;  // [NS]
-
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-
-  // ---- work item -> (sequence, unit, token range)
-  const int item = blockIdx.x;
-  const int cg = item / p.units;
-  const int unit = item - cg * p.units;
-  int b, c, seq_len;
+// Work item (blockIdx.x) -> sequence b, chunk c of it, the sequence's length.
+// Returns false when the item has no chunk (paged bound past the call's count).
+// seq_s: three ints of shared scratch (paged calls).
+template <bool PAGED>
+__device__ __forceinline__ bool resolve_item(const DecodeParams& p, int cg, int& b, int& c, int& seq_len,
+                                             int* seq_s) {
   if (PAGED) {
     grid_dep_wait();  // chunk offsets come from the planner kernel
     const int total = p.chunk_offset[p.B + 1], full = p.chunk_offset[p.B];
-    if (cg >= total) return;
+    if (cg >= total) return false;
     if (cg >= full) {  // a partial last chunk, after every full one
       b = p.tail_seq[cg - full];
       seq_len = paged_seq_len(p, b);
@@ -233,7 +235,6 @@ __global__ void __launch_bounds__(kDecodeThreads, (G * D > 512) ? 2 : 3) decode_
       // chunk range holds cg (exactly one; empty ranges never match) publishes
       // itself, the chunk index and its length (a binary search is a chain of
       // dependent loads ahead of the CTA's first copy)
-      __shared__ int seq_s[3];
       const int t = threadIdx.x;
       if (t < p.B) {
         const int a = p.chunk_offset[t], z = p.chunk_offset[t + 1];
@@ -263,6 +264,38 @@ __global__ void __launch_bounds__(kDecodeThreads, (G * D > 512) ? 2 : 3) decode_
     c = cg - b * p.chunks_per_seq;
     seq_len = p.L;
   }
+  return true;
+}
+
+template <typename T, int D, int G, bool PAGED>
+__global__ void __launch_bounds__(kDecodeThreads, (G * D > 512) ? 2 : 3) decode_splitkv_kernel(const DecodeParams p) {
+  static_assert(D % 64 == 0 && D <= 256, "head_dim");
+  static_assert(G == 1 || G == 2 || G == 4 || G == 8, "group tile");
+  using E = Elem<T>;
+
+  extern __shared__ __align__(128) unsigned char smem[];
+  const int NS = p.num_stages;
+  const int TT = p.tile_tokens;
+  const int stage_elems = TT * D;
+  T* kv_s = reinterpret_cast<T*>(smem);  // [NS][2][TT][D]
+  float* comb = reinterpret_cast<float*>(smem + (size_t)NS * 2 * stage_elems * sizeof(T));
+  float* comb_m = comb;                               // [NW][G]
+  float* comb_l = comb_m + kConsumerWarps * G;        // [NW][G]
+  float* comb_o = comb_l + kConsumerWarps * G;        // [NW][G][D]
+  float* p_s = comb_o + kConsumerWarps * G * D;       // [NW][kSubTile][G]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(p_s + kConsumerWarps * kSubTile * G);
+  uint64_t* full = bars;        // [NS]
+  uint64_t* empty = bars + NS;  // [NS]
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  // ---- work item -> (sequence, unit, token range)
+  const int item = blockIdx.x;
+  const int cg = item / p.units;
+  const int unit = item - cg * p.units;
+  int b, c, seq_len;
+  __shared__ int seq_s[3];
+  if (!resolve_item<PAGED>(p, cg, b, c, seq_len, seq_s)) return;
   const int tok_begin = c * p.chunk_tokens;
   const int tok_end = min(seq_len, tok_begin + p.chunk_tokens);
   const int n_tiles = cdiv(tok_end - tok_begin, TT);
@@ -369,19 +402,181 @@ __global__ void __launch_bounds__(kDecodeThreads, (G * D > 512) ? 2 : 3) decode_
   // ---- combine the consumer warps' states
   wa.stash(comb_m, comb_l, comb_o, cw, alive);
   named_bar_sync(1, kConsumerWarps * 32);
-  const int ctid = threadIdx.x - 32 * kProducerWarps;
-  T* out = static_cast<T*>(p.out);
-  for (int e = ctid; e < G * D; e += kConsumerWarps * 32) {
-    const int h = e / D, d = e - h * D;
-    float lse2;
-    const float val = combine_warps<kConsumerWarps, G, D>(comb_m, comb_l, comb_o, h, d, lse2);
-    if (p.direct_out) {
-      out[(int64_t)b * p.o_sb + (int64_t)(head0 + h) * p.o_sh + (int64_t)d * p.o_sd] = E::from_float(val);
-    } else {
-      p.part_o[((int64_t)item * G + h) * D + d] = val;
-      if (d == 0) p.part_lse[(int64_t)item * G + h] = lse2;
-    }
+  write_item<T, D, G>(p, item, b, head0, comb_m, comb_l, comb_o, threadIdx.x - 32 * kProducerWarps);
+}
+
+// ---------------------------------------------------------------------------
+// Split-KV decode on the tensor cores: the same work items, chunk order,
+// producer ring and combine as decode_splitkv_kernel, with
+//  * the producer loading each tile through two 4-D tensor maps (K and V:
+//    [D, tokens, kv heads, pages or sequences]) with a 128-byte swizzle, one
+//    64-column box per half of D, so the consumers' ldmatrix reads are free of
+//    bank conflicts (the 1-D bulk copies land rows 256 bytes apart, which puts
+//    the 8 rows an ldmatrix phase reads in the same banks);
+//  * consumer warps running WarpMma (16 keys per step, two m16n8k16 products)
+//    instead of the CUDA-core warp core.
+// A tile is TT keys (a multiple of 16).  The box always moves TT rows: rows past
+// the sequence end inside a page are the pool's own bytes, so a consumer
+// zeroes those V rows before its step (a masked key's p is 0, and 0 * NaN is
+// NaN on the tensor cores too); dense rows past L are filled with zeros by the
+// tensor-map load.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void tma_load_4d_hint(void* dst, const CUtensorMap* map, int x, int y, int z, int w,
+                                                 uint64_t* bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1, "
+      "{%3, %4, %5, %6}], [%2], %7;" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z), "r"(w), "l"(policy)
+      : "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+template <typename T, int D, int G, bool PAGED>
+__global__ void __launch_bounds__(kDecodeThreads, 3)
+    decode_mma_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+                      const DecodeParams p) {
+  static_assert(D % 64 == 0 && D <= 256, "head_dim");
+  // Stages on 1024-byte boundaries: the tensor-map loads' 128-byte swizzle
+  // repeats every 1024 bytes.  The kernel declares no static shared memory,
+  // so the dynamic region starts the CTA's window; the check below reads its
+  // address through an opaque move (the declared alignment would let the
+  // compiler drop a plain test) and stops the CTA before any load if it is off.
+  extern __shared__ __align__(1024) unsigned char smem_tc[];
+  unsigned char* smem = smem_tc;
+  uint32_t smem_base;
+  asm volatile("mov.b32 %0, %1;" : "=r"(smem_base) : "r"(smem_u32(smem_tc)));
+  const int NS = p.num_stages;
+  const int TT = p.tile_tokens;
+  const int stage_elems = TT * D;  // one matrix of a stage: [D / 64][TT][64]
+  const uint32_t mat_bytes = (uint32_t)stage_elems * sizeof(T);
+  const uint32_t half_bytes = (uint32_t)TT * 128u;
+  T* kv_s = reinterpret_cast<T*>(smem);  // [NS][2][D / 64][TT][64]
+  float* comb_m = reinterpret_cast<float*>(smem + (size_t)NS * 2 * mat_bytes);  // [NW][G]
+  float* comb_l = comb_m + kConsumerWarps * G;                                 // [NW][G]
+  float* comb_o = comb_l + kConsumerWarps * G;                                 // [NW][G][D]
+  uint64_t* full = reinterpret_cast<uint64_t*>(comb_o + kConsumerWarps * G * D);  // [NS]
+  uint64_t* empty = full + NS;                                                    // [NS]
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int item = blockIdx.x;
+  const int cg = item / p.units;
+  const int unit = item - cg * p.units;
+  int b, c, seq_len;
+  // the lookup's scratch: the first ints of comb_m (written only at the end)
+  if (!resolve_item<PAGED>(p, cg, b, c, seq_len, reinterpret_cast<int*>(comb_m))) return;
+  const int tok_begin = c * p.chunk_tokens;
+  const int tok_end = min(seq_len, tok_begin + p.chunk_tokens);
+  const int n_tiles = cdiv(tok_end - tok_begin, TT);
+  const int kvh = unit / p.g_tiles;
+  const int head0 = kvh * p.group + (unit - kvh * p.g_tiles) * G;
+
+  if (NS % kConsumerWarps != 0 || (TT & 15) != 0 || (smem_base & 1023u) != 0) {  // host guarantees these
+    if (threadIdx.x == 0) record_status(kStatusWaitTimeout);
+    return;
   }
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  if (warp < kProducerWarps) {
+    // ======================= producer =======================
+    const uint64_t pol = l2_policy_evict_first();
+    int page_base = 0, npages = 0, batch_lo = -1, my_pid = -1, issued = 0;
+    if (PAGED) {
+      page_base = p.indptr[b];
+      npages = p.indptr[b + 1] - page_base;
+    }
+    for (int t = 0; t < n_tiles; ++t) {
+      const int slot = t % NS;
+      const uint32_t phase = (uint32_t)(t / NS) & 1u;
+      const int tok = tok_begin + t * TT;
+      int y, w;  // token coordinate inside the page / sequence; page id / sequence
+      bool ok_addr = true;
+      if (PAGED) {
+        const int pl = tok / p.P;
+        if (batch_lo < 0 || pl >= batch_lo + 32) {
+          batch_lo = pl;
+          const int j = batch_lo + lane;
+          my_pid = (j < npages) ? __ldg(p.indices + page_base + j) : -1;
+        }
+        const int pid = __shfl_sync(0xffffffffu, my_pid, pl - batch_lo);
+        ok_addr = pid >= 0 && (int64_t)pid < p.num_pages;
+        y = tok - pl * p.P;
+        w = pid;
+      } else {
+        y = tok;
+        w = b;
+      }
+      bool ok = true;
+      if (t >= NS && lane == 0) ok = mbar_wait(&empty[slot], phase ^ 1u);
+      if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) break;
+      issued = t + 1;
+      if (lane == 0) {
+        T* dst = kv_s + (size_t)slot * 2 * stage_elems;
+        if (ok_addr) {
+          mbar_arrive_expect_tx(&full[slot], 2u * mat_bytes);
+#pragma unroll
+          for (int hh = 0; hh < D / 64; ++hh) {
+            tma_load_4d_hint(dst + hh * TT * 64, &tmK, hh * 64, y, kvh, w, &full[slot], pol);
+            tma_load_4d_hint(dst + stage_elems + hh * TT * 64, &tmV, hh * 64, y, kvh, w, &full[slot], pol);
+          }
+        } else {
+          record_status(kStatusBadPage);
+          mbar_arrive(&full[slot]);
+        }
+      }
+      __syncwarp();
+    }
+    // no exit while tensor-map loads into this CTA's shared memory are in
+    // flight (bounded waits; returns at once on the normal path)
+    if (lane == 0) {
+      for (int t = max(0, issued - NS); t < issued; ++t) mbar_wait(&full[t % NS], (uint32_t)(t / NS) & 1u);
+    }
+    return;
+  }
+
+  // ========================= consumers =========================
+  const int cw = warp - kProducerWarps;
+  WarpMma<T, D, G> wm;
+  wm.init(lane);
+  wm.load_q(static_cast<const T*>(p.q) + (int64_t)b * p.q_sb + (int64_t)head0 * p.q_sh, p.q_sh);
+  bool alive = true;
+  for (int t = cw; t < n_tiles; t += kConsumerWarps) {
+    const int slot = t % NS;
+    if (!mbar_wait(&full[slot], (uint32_t)(t / NS) & 1u)) { alive = false; break; }
+    const int n = min(TT, tok_end - (tok_begin + t * TT));
+    T* ks = kv_s + (size_t)slot * 2 * stage_elems;
+    const uint32_t kb = smem_u32(ks);
+    bool zeroed = false;
+    if (PAGED && n < TT) {
+      // rows n..TT-1 of V: whole 128-byte rows of every half
+      unsigned char* vg = reinterpret_cast<unsigned char*>(ks + stage_elems);
+      const int per_half = (TT - n) * 8;
+      for (int e = lane; e < per_half * (D / 64); e += 32) {
+        const int hh = e / per_half, r = e - hh * per_half;
+        *reinterpret_cast<uint4*>(vg + hh * half_bytes + (n + (r >> 3)) * 128 + (r & 7) * 16) = make_uint4(0, 0, 0, 0);
+      }
+      __syncwarp();
+      zeroed = true;
+    }
+    for (int sub = 0; sub < n; sub += 16)
+      wm.step(kb, kb + mat_bytes, half_bytes, sub, min(16, n - sub), p.scale_log2);
+    __syncwarp();
+    if (zeroed) fence_proxy_async_smem();  // generic writes before the next tensor-map load of the slot
+    if (lane == 0) mbar_arrive(&empty[slot]);
+  }
+
+  wm.stash(comb_m, comb_l, comb_o, cw, alive);
+  named_bar_sync(1, kConsumerWarps * 32);
+  write_item<T, D, G>(p, item, b, head0, comb_m, comb_l, comb_o, threadIdx.x - 32 * kProducerWarps);
 }
 
 // ---------------------------------------------------------------------------
@@ -487,7 +682,9 @@ struct Plan {
   int G_tile, tile_tokens, chunk_tokens, num_stages;
   int64_t items;  // upper bound (paged) or exact (dense)
   int chunks_per_seq;
-  size_t smem;
+  size_t smem;     // CUDA-core kernel
+  size_t smem_tc;  // tensor-core kernel
+  bool tc;         // tiles fit the tensor-core kernel (a multiple of 16 keys)
   size_t ws_bytes;
   size_t off_lse, off_chunk;
   bool direct;
@@ -538,6 +735,16 @@ int env_int(const char* name, int dflt) {
   return *slot;
 }
 
+// AKT_DECODE_TENSOR_CORES=0 selects the CUDA-core split-KV kernel for every
+// call (default: the tensor-core kernel wherever the tiles fit it).
+bool use_tensor_cores() {
+  static const bool on = [] {
+    const char* v = getenv("AKT_DECODE_TENSOR_CORES");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
+
 int pick_group_tile(int group, int D) {
   const int cap = D >= 256 ? 4 : 8;
   for (int g = cap; g >= 2; g >>= 1)
@@ -567,6 +774,14 @@ Plan make_plan(bool paged, int B, int Hq, int Hkv, int D, int L, int P, int64_t 
   // tokens at P=16, already two stages per warp.)
   const int dense_split = std::max(1, tcap / std::max(kSubTile, tcap / 2));
   pl.tile_tokens = paged ? largest_divisor_le(P, tcap) : tcap / dense_split;
+  // The tensor-core kernel takes tiles of a multiple of 16 keys: the largest
+  // such divisor of the page (pages of a multiple of 16 keys; others keep the
+  // CUDA-core kernel).  Dense tiles are 16 or 32 keys already.
+  if (paged && P % 16 == 0) {
+    for (int d = (tcap / 16) * 16; d >= 16; d -= 16)
+      if (P % d == 0) { pl.tile_tokens = d; break; }
+  }
+  pl.tc = pl.tile_tokens % 16 == 0 && use_tensor_cores();
   const size_t stage_bytes = (size_t)2 * pl.tile_tokens * D * elem_size;
   // Consumer warp w takes tiles w, w+NW, ...; with NS a multiple of NW every
   // slot has one fixed consumer, so each mbarrier is waited phase by phase
@@ -619,22 +834,68 @@ Plan make_plan(bool paged, int B, int Hq, int Hkv, int D, int L, int P, int64_t 
   pl.smem = (size_t)pl.num_stages * stage_bytes +
             sizeof(float) * ((size_t)kConsumerWarps * pl.G_tile * (2 + D) + (size_t)kConsumerWarps * kSubTile * pl.G_tile) +
             sizeof(uint64_t) * 2 * pl.num_stages;
+  pl.smem_tc = (size_t)pl.num_stages * stage_bytes + sizeof(float) * (size_t)kConsumerWarps * pl.G_tile * (2 + D) +
+               sizeof(uint64_t) * 2 * pl.num_stages;
   layout_workspace(pl, paged, B, units, D, L, P, num_page_entries);
   return pl;
 }
 
+// K and V tensor maps of the tensor-core kernel: [D, tokens, kv heads, pages]
+// (paged) or [D, L, kv heads, sequences] (dense), 64 x TT boxes, 128-byte
+// swizzle; rows past L read as zeros.  False when a map cannot be made
+// (the caller then runs the CUDA-core kernel).
+template <typename T>
+bool decode_maps(CUtensorMap& mk, CUtensorMap& mv, const DecodeParams& p, bool paged, int D, int TT) {
+  const auto fn = tensor_map_encoder();
+  if (!fn) return false;
+  const int64_t outer = paged ? p.num_pages : p.B;
+  const int64_t toks = paged ? p.P : p.L;
+  if (outer <= 0 || toks <= 0 || TT > 256) return false;
+  const cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)toks, (cuuint64_t)p.Hkv, (cuuint64_t)outer};
+  const int64_t st[3] = {p.s_tok * 2, p.s_head * 2, p.s0 * 2};
+  cuuint64_t strides[3];
+  for (int i = 0; i < 3; ++i) {
+    if (st[i] <= 0 || (st[i] & 15) || st[i] >= (int64_t(1) << 40)) return false;
+    strides[i] = (cuuint64_t)st[i];
+  }
+  if ((reinterpret_cast<uintptr_t>(p.k) & 15) || (reinterpret_cast<uintptr_t>(p.v) & 15)) return false;
+  const cuuint32_t box[4] = {64, (cuuint32_t)TT, 1, 1};
+  const cuuint32_t es[4] = {1, 1, 1, 1};
+  const CUtensorMapDataType dt =
+      std::is_same<T, __half>::value ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  for (int m = 0; m < 2; ++m) {
+    const CUresult r = fn(m == 0 ? &mk : &mv, dt, 4, const_cast<void*>(m == 0 ? p.k : p.v), dims, strides, box, es,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return false;
+  }
+  return true;
+}
+
 template <typename T, int D, int G, bool PAGED>
 int launch_decode(DecodeParams p, const Plan& pl, cudaStream_t st) {
-  auto kern = decode_splitkv_kernel<T, D, G, PAGED>;
-  cudaError_t e = ensure_smem_limit<decode_splitkv_kernel<T, D, G, PAGED>>(pl.smem);
+  CUtensorMap mk, mv;
+  const bool tc = pl.tc && pl.items > 0 && decode_maps<T>(mk, mv, p, PAGED, D, pl.tile_tokens);
+  cudaError_t e = tc ? ensure_smem_limit<decode_mma_kernel<T, D, G, PAGED>>(pl.smem_tc)
+                     : ensure_smem_limit<decode_splitkv_kernel<T, D, G, PAGED>>(pl.smem);
   if (e != cudaSuccess) return set_error(AKT_ERR_CUDA, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
   if (PAGED) paged_plan_kernel<<<1, 1024, 0, st>>>(p);
   if (pl.items > 0) {
     ProfileScope prof(st);
-    if (PAGED)  // after the planner: may start while it runs
-      e = launch_dependent(kern, dim3((unsigned)pl.items), dim3(kDecodeThreads), pl.smem, st, p);
-    else
-      kern<<<(unsigned)pl.items, kDecodeThreads, pl.smem, st>>>(p);
+    const dim3 grid((unsigned)pl.items), block(kDecodeThreads);
+    if (tc) {
+      auto kern = decode_mma_kernel<T, D, G, PAGED>;
+      if (PAGED)  // after the planner: may start while it runs
+        e = launch_dependent(kern, grid, block, pl.smem_tc, st, mk, mv, p);
+      else
+        kern<<<grid, block, pl.smem_tc, st>>>(mk, mv, p);
+    } else {
+      auto kern = decode_splitkv_kernel<T, D, G, PAGED>;
+      if (PAGED)
+        e = launch_dependent(kern, grid, block, pl.smem, st, p);
+      else
+        kern<<<grid, block, pl.smem, st>>>(p);
+    }
     if (e != cudaSuccess) return set_error(AKT_ERR_CUDA, std::string("decode launch: ") + cudaGetErrorString(e));
   }
   if (!pl.direct) {  // the merge (also zeros for a dense call over no keys or an empty sequence)

@@ -41,6 +41,7 @@
 #define AKT_WHOLE_PROGRAM 1
 #include "common.cuh"
 #include "profile.cuh"
+#include "tensor_map.h"
 
 #include <cuda.h>
 #include <cudaTypedefs.h>
@@ -823,18 +824,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 // -------------------------------------------------------------------------
 // host: tensor maps through the driver entry point (no -lcuda)
 // -------------------------------------------------------------------------
-PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* f = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
-  });
-  return fn;
-}
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() { return tensor_map_encoder(); }
 
 // 4-D map over [B][H][S][D] (element strides sb, sh, ss; dim stride 1), box 64 x 128
 int make_map(CUtensorMap* m, const void* base, int dtype, int B, int H, int S, int D, int64_t sb, int64_t sh,

@@ -40,7 +40,13 @@ from attention_kernel_triton_b200 import workloads as W  # noqa: E402
 
 METRIC = "paged decode HBM GB/s"
 GRAPH_STEPS = 16  # e2e steps per captured CUDA graph
-CFG3_TRAFFIC_BYTES = 4.51e9 + 7.19e6  # ncu: read 4.51 GB + write 7.19 MB per split-KV launch
+# DRAM bytes of one split-KV launch on cfg3.  Tensor-core kernel: ncu on the
+# 8-sequence case (--batch 8: read 437.648 MB + write 3.849 MB for 437.439 MB of
+# algorithmic bytes) scaled to cfg3's 4513.9 MB by the algorithmic bytes (reads
+# grow with the tokens; the partials' writes grow more slowly, so this bounds
+# them from above).  CUDA-core kernel: ncu on cfg3 itself (4.51 GB + 7.19 MB).
+CFG3_TRAFFIC_BYTES = (437.648e6 + 3.849e6) / 437.439e6 * 4513.900124e6
+CFG3_TRAFFIC_BYTES_CUDA_CORES = 4.51e9 + 7.19e6
 WORKLOAD = ("cfg3 paged var-len GQA decode: B=64 Hq=32 Hkv=8 D=128 fp16 page_size=16 "
             "lens U[512,32768] seeded, random physical page order")
 
@@ -790,6 +796,8 @@ def run_ours(args):
             cpu = {"value": sbytes / cpu_t / 1e9, "unit": "GB/s", "cores": threads, "kind": "port",
                    "sample": f"naive_paged_attention restated (oracle port), fp32 torch CPU, first "
                              f"{args.cpu_seqs} cfg3 sequences, mean of 2 runs"}
+        cfg3_traffic = (CFG3_TRAFFIC_BYTES_CUDA_CORES
+                        if os.environ.get("AKT_DECODE_TENSOR_CORES", "1").startswith("0") else CFG3_TRAFFIC_BYTES)
         result = {
             "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
@@ -800,12 +808,16 @@ def run_ours(args):
                        "parallelism": f"independent batch per GPU x{world}"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_source": peak_kind,
-                         "kernel": "decode_splitkv_kernel<half,128,4,paged>",
+                         # cfg3's pages (16 keys) take the tensor-core split-KV kernel unless it is
+                         # switched off for the call's process
+                         "kernel": ("decode_splitkv_kernel<half,128,4,paged>"
+                                    if os.environ.get("AKT_DECODE_TENSOR_CORES", "1").startswith("0")
+                                    else "decode_mma_kernel<half,128,4,paged>"),
                          "kernel_ms": kern_ms,
                          # dram__bytes_read.sum + dram__bytes_write.sum of one launch of this
-                         # kernel on this workload, from an ncu capture of the same command
-                         "traffic": CFG3_TRAFFIC_BYTES if args.batch == 64 else None,
-                         "traffic_over_algorithmic": CFG3_TRAFFIC_BYTES / nbytes if args.batch == 64 else None},
+                         # kernel on this workload (ncu; see CFG3_TRAFFIC_BYTES)
+                         "traffic": cfg3_traffic if args.batch == 64 else None,
+                         "traffic_over_algorithmic": cfg3_traffic / nbytes if args.batch == 64 else None},
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_val, "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "ms_per_step": e2e_ms, "host_issue_ms_per_step": host_ms,

@@ -147,6 +147,23 @@ def test_paged_decode_reference_assert(monkeypatch):
                                      cuda(c.last_page_len))
 
 
+@pytest.mark.parametrize("D,P", [(128, 16), (64, 64), (256, 32)])
+def test_paged_decode_nan_past_last_token(D, P):
+    # The tensor-core kernel moves whole 16-key tiles of a page; the pool slots
+    # past a sequence's last token are not the sequence's data and may hold
+    # anything (here NaN, in K and V).  They must not reach the output.
+    c = W.make_paged(Hq=8, Hkv=2, D=D, page_size=P, lens=[1, 17, P + 3, 5 * P - 1], seed=D + P)
+    cache = c.cache.clone()
+    for b in range(len(c.last_page_len)):
+        s, e = int(c.indptr[b]), int(c.indptr[b + 1])
+        last = int(c.last_page_len[b])
+        if e > s and last < P:
+            cache[int(c.indices[e - 1]), :, :, last:, :] = float("nan")
+    O = flash_attention_decode_paged(cuda(c.q), cuda(cache), cuda(c.indptr), cuda(c.indices),
+                                     cuda(c.last_page_len))
+    check_close(O, N.naive_paged_attention(c.q, c.cache, c.indptr, c.indices, c.last_page_len))
+
+
 def test_paged_decode_last_page_len_clamped():
     c = W.make_paged(Hq=4, Hkv=2, D=64, page_size=16, lens=[40, 16], seed=5)
     last = c.last_page_len.clone()
