@@ -14,8 +14,9 @@
 //    positions).  A one-CTA planner turns nnz into per-unit chunk counts and
 //    offsets; persistent CTAs walk the item list; a merge kernel combines the
 //    per-chunk (O, log2-sum-exp) partials of each head.
-//  * Gather: each kept row of K and V is one 1-D bulk copy (TMA engine)
-//    HBM->shared, issued by one thread per row, completing one mbarrier.
+//  * Gather: 32 threads resolve one kept row each to an element offset (the
+//    page-table lookup for paged K/V); then all threads load the rows' 16-byte
+//    pieces with streaming loads into shared memory.
 //  * GQA: the index lists are per qo head in the API.  When the G heads of an
 //    item carry identical positions (the common case: a per-kv-head keep mask
 //    repeated over the group) the rows are gathered once and all G heads are
@@ -182,9 +183,19 @@ struct MagicPigScore {
     c = fminf(fmaxf(c, -1.0f + 1e-7f), 1.0f - 1e-7f);
     float pr = 1.0f - (1.0f / kPi) * acosf(c);
     pr = fminf(fmaxf(pr, 0.0f), 1.0f);
-    const float pK = powf(pr, K);
+    // p^K and (1-p^K)^(L-1) as exp2(e * log2(base)) through CUDA's exp2f and
+    // log2f, and (1-p^K)^L as (1-p^K) * (1-p^K)^(L-1): one logarithm and one
+    // exponential per power instead of three powf calls.  A zero base keeps
+    // powf, for its special cases (0^0 = 1, 0 to a negative power).
+    const float pK = pr > 0.f ? exp2f(K * log2f(pr)) : powf(pr, K);
     const float omp = fminf(fmaxf(1.0f - pK, 0.0f), 1.0f);
-    float u = 1.0f - powf(omp, Lp) - Lp * pK * powf(omp, Lp - 1.0f);
+    float u;
+    if (omp > 0.f) {
+      const float y = exp2f((Lp - 1.0f) * log2f(omp));  // (1-p^K)^(L-1)
+      u = 1.0f - y * (omp + Lp * pK);
+    } else {
+      u = 1.0f - powf(omp, Lp) - Lp * pK * powf(omp, Lp - 1.0f);
+    }
     u = fmaxf(u, 1e-10f);
     return (dot * inv_sqrt_d - logf(u)) * kLog2e;
   }
