@@ -582,12 +582,16 @@ __global__ void __launch_bounds__(kDecodeThreads, 3)
 // ---------------------------------------------------------------------------
 // merge of split-KV partials: O = sum_j 2^{lse_j - M} O_j / sum_j 2^{lse_j - M}
 // One CTA per (sequence, unit).  Per head, one warp takes the max and the sum
-// of 2^(lse_j - M) over the chunks (lanes striding the chunks); then each
-// thread accumulates four consecutive dims of one head (one 16-byte load per
-// chunk, chunks unrolled so several loads are in flight).
+// of 2^(lse_j - M) over the chunks (lanes striding the chunks).  Then the
+// threads form blockDim / (G * D / 4) groups; in each group a thread
+// accumulates four consecutive dims of one head over every groups-th chunk
+// (one 16-byte load per chunk, unrolled so several loads are in flight), and
+// the groups' sums are added in shared memory.  The host launches 1024
+// threads when the chunk lists are long (16 chunks or more per pair; a
+// single long sequence has ~50), and 256 otherwise.
 // ---------------------------------------------------------------------------
 template <typename T, int D, int G, bool PAGED>
-__global__ void __launch_bounds__(256) decode_merge_kernel(const DecodeParams p) {
+__global__ void __launch_bounds__(1024) decode_merge_kernel(const DecodeParams p) {
   using E = Elem<T>;
   grid_dep_wait();  // partials (and chunk offsets) of the previous kernels
   const int b = blockIdx.x / p.units;
@@ -609,7 +613,10 @@ __global__ void __launch_bounds__(256) decode_merge_kernel(const DecodeParams p)
   const int head0 = kvh * p.group + (unit - kvh * p.g_tiles) * G;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   __shared__ float head_m[G], head_inv[G];
-  for (int h = warp; h < G; h += 8) {
+  constexpr int NE = G * D / 4;  // four-dim elements of the unit's output
+  static_assert(NE <= 256, "elements per unit");
+  __shared__ float4 red[1024 - NE];  // sums of groups 1.. (blockDim <= 1024)
+  for (int h = warp; h < G; h += (int)(blockDim.x >> 5)) {
     float m = -INFINITY;
     for (int k = lane; k < nc; k += 32) m = fmaxf(m, p.part_lse[((int64_t)chunk(k) * p.units + unit) * G + h]);
 #pragma unroll
@@ -626,14 +633,15 @@ __global__ void __launch_bounds__(256) decode_merge_kernel(const DecodeParams p)
     }
   }
   __syncthreads();
-  T* out = static_cast<T*>(p.out);
-  for (int e = 4 * threadIdx.x; e < G * D; e += 4 * blockDim.x) {
-    const int h = e / D, d = e - h * D;
+  const int groups = max(1, (int)blockDim.x / NE);
+  const int gi = threadIdx.x / NE, e4 = threadIdx.x - gi * NE;
+  float4 num = make_float4(0.f, 0.f, 0.f, 0.f);
+  const int h = (4 * e4) / D, d = 4 * e4 - h * D;
+  if (gi < groups) {
     const float M = head_m[h];
-    float4 num = make_float4(0.f, 0.f, 0.f, 0.f);
     if (M != -INFINITY) {
 #pragma unroll 8
-      for (int k = 0; k < nc; ++k) {
+      for (int k = gi; k < nc; k += groups) {
         const int64_t it = (int64_t)chunk(k) * p.units + unit;
         const float w = fast_exp2(p.part_lse[it * G + h] - M);
         const float4 o = *reinterpret_cast<const float4*>(p.part_o + (it * G + h) * D + d);
@@ -643,7 +651,19 @@ __global__ void __launch_bounds__(256) decode_merge_kernel(const DecodeParams p)
         num.w += w * o.w;
       }
     }
+    if (gi > 0) red[(gi - 1) * NE + e4] = num;
+  }
+  if (groups > 1) __syncthreads();
+  if (gi == 0) {
+    for (int g2 = 1; g2 < groups; ++g2) {
+      const float4 o = red[(g2 - 1) * NE + e4];
+      num.x += o.x;
+      num.y += o.y;
+      num.z += o.z;
+      num.w += o.w;
+    }
     const float inv = head_inv[h];
+    T* out = static_cast<T*>(p.out);
     T* orow = out + (int64_t)b * p.o_sb + (int64_t)(head0 + h) * p.o_sh;
     orow[(int64_t)d * p.o_sd] = E::from_float(num.x * inv);
     orow[(int64_t)(d + 1) * p.o_sd] = E::from_float(num.y * inv);
@@ -900,7 +920,11 @@ int launch_decode(DecodeParams p, const Plan& pl, cudaStream_t st) {
   }
   if (!pl.direct) {  // the merge (also zeros for a dense call over no keys or an empty sequence)
     const unsigned nb = (unsigned)p.B * p.units;
-    if (nb > 0) e = launch_dependent(decode_merge_kernel<T, D, G, PAGED>, dim3(nb), dim3(256), 0, st, p);
+    // long chunk lists (dense: the chunk count; paged: the planner's bound per
+    // sequence, on average) are split over 1024 threads, short ones over 256
+    const int64_t per_pair = PAGED ? pl.items / std::max(1, p.units) / std::max(1, p.B) : pl.chunks_per_seq;
+    const unsigned mthreads = per_pair >= 16 ? 1024u : 256u;
+    if (nb > 0) e = launch_dependent(decode_merge_kernel<T, D, G, PAGED>, dim3(nb), dim3(mthreads), 0, st, p);
     if (e != cudaSuccess) return set_error(AKT_ERR_CUDA, std::string("decode merge launch: ") + cudaGetErrorString(e));
   }
   e = cudaGetLastError();
