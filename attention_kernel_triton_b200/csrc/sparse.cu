@@ -506,10 +506,16 @@ __device__ __forceinline__ void store4(float* dst, float4 v) {
 // merge of the per-chunk partials of every (batch, unit): chunks are the
 // contiguous items unit_offset[u] .. unit_offset[u+1).  Per head, one warp
 // takes the max and the sum of 2^(lse - max) over the chunks (lanes striding
-// the chunks); then each thread accumulates four consecutive dims of one head
-// (one 16-byte load per chunk, chunks unrolled so several loads are in flight).
-template <typename T, int D, int G>
-__global__ void __launch_bounds__(256) sparse_merge_kernel(const SparseParams p) {
+// the chunks).  Then the NT threads form NT / (G * D / 4) groups; in each group
+// a thread accumulates four consecutive dims of one head over every
+// groups-th chunk (one 16-byte load per chunk, unrolled so several loads are
+// in flight), and the groups' sums are added in shared memory.  NT = 1024 on
+// the single-device path when the (batch, unit) pairs fit one wave (their
+// chunk lists are then long: ~80 per pair for one 128K sequence); 256
+// otherwise, and always with the peer exchange, whose fused final merge
+// relies on four CTAs of this kernel being resident per SM.
+template <typename T, int D, int G, int NT>
+__global__ void __launch_bounds__(NT, NT == 256 ? 4 : 1) sparse_merge_kernel(const SparseParams p) {
   using E = Elem<T>;
   grid_dep_wait();  // partials (and item offsets) of the previous kernels
   const int u = blockIdx.x;
@@ -519,7 +525,11 @@ __global__ void __launch_bounds__(256) sparse_merge_kernel(const SparseParams p)
   const int i0 = p.unit_offset[u], i1 = p.unit_offset[u + 1];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   __shared__ float head_m[G], head_den[G];
-  for (int h = warp; h < G; h += 8) {
+  constexpr int NE = G * D / 4;  // four-dim elements of the unit's output
+  static_assert(NT % NE == 0, "groups");
+  constexpr int kGroups = NT / NE;
+  __shared__ float4 red[kGroups > 1 ? (kGroups - 1) * NE : 1];  // sums of groups 1..
+  for (int h = warp; h < G; h += NT / 32) {
     float m = -INFINITY;
     for (int it = i0 + lane; it < i1; it += 32) m = fmaxf(m, p.part_lse[(int64_t)it * G + h]);
 #pragma unroll
@@ -537,13 +547,14 @@ __global__ void __launch_bounds__(256) sparse_merge_kernel(const SparseParams p)
   __syncthreads();
   T* out = static_cast<T*>(p.out);
   const int64_t rows = (int64_t)p.B * p.Hq;
-  for (int e = 4 * threadIdx.x; e < G * D; e += 4 * blockDim.x) {
-    const int h = e / D, d = e - h * D;
-    const float M = head_m[h], den = head_den[h];
-    float4 num = make_float4(0.f, 0.f, 0.f, 0.f);
+  const int gi = threadIdx.x / NE, e4 = threadIdx.x - gi * NE;
+  float4 num = make_float4(0.f, 0.f, 0.f, 0.f);
+  {
+    const int h = (4 * e4) / D, d = 4 * e4 - h * D;
+    const float M = head_m[h];
     if (M != -INFINITY) {
 #pragma unroll 8
-      for (int it = i0; it < i1; ++it) {
+      for (int it = i0 + gi; it < i1; it += kGroups) {
         const float w = fast_exp2(p.part_lse[(int64_t)it * G + h] - M);
         const float4 o = *reinterpret_cast<const float4*>(p.part_o + ((int64_t)it * G + h) * D + d);
         num.x += w * o.x;
@@ -551,6 +562,20 @@ __global__ void __launch_bounds__(256) sparse_merge_kernel(const SparseParams p)
         num.z += w * o.z;
         num.w += w * o.w;
       }
+    }
+    if (kGroups > 1 && gi > 0) red[(gi - 1) * NE + e4] = num;
+  }
+  if (kGroups > 1) __syncthreads();
+  if (gi == 0) {
+    const int h = (4 * e4) / D, d = 4 * e4 - h * D;
+    const float M = head_m[h], den = head_den[h];
+#pragma unroll
+    for (int g2 = 1; g2 < kGroups; ++g2) {
+      const float4 o = red[(g2 - 1) * NE + e4];
+      num.x += o.x;
+      num.y += o.y;
+      num.z += o.z;
+      num.w += o.w;
     }
     const float inv = den > 0.f ? 1.f / den : 0.f;
     const float4 val = make_float4(num.x * inv, num.y * inv, num.z * inv, num.w * inv);
@@ -688,7 +713,18 @@ template <typename T, int D, int G, bool PAGED, bool MAGIC>
 int launch_sparse(const SparseParams& p, const SparsePlan& pl, cudaStream_t st) {
   auto kern = sparse_decode_kernel<T, D, G, PAGED, MAGIC>;
   const size_t smem = SparseSmem<T, D, G>::bytes;
-  cudaError_t e = ensure_smem_limit<sparse_decode_kernel<T, D, G, PAGED, MAGIC>>(smem);
+  cudaError_t e;
+  if (p.final_merge && p.B * p.units > 0) {
+    // the fused final merge waits on its own grid: every CTA must be resident
+    // (checked before anything is launched, so a refusal leaves no partial
+    // exchange behind)
+    int per_sm = 0;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, sparse_merge_kernel<T, D, G, 256>, 256, 0);
+    if (e != cudaSuccess) return set_error(AKT_ERR_CUDA, std::string("occupancy query: ") + cudaGetErrorString(e));
+    if ((int64_t)p.B * p.units > (int64_t)per_sm * sm_count())
+      return set_error(AKT_ERR_UNSUPPORTED, "split_peer: the merge grid does not fit the GPU at once");
+  }
+  e = ensure_smem_limit<sparse_decode_kernel<T, D, G, PAGED, MAGIC>>(smem);
   if (e != cudaSuccess) return set_error(AKT_ERR_CUDA, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
   // One resident wave of CTAs walks the items (the count is an upper bound
   // from the list capacity; the planner finds the real one on the device).
@@ -712,7 +748,12 @@ int launch_sparse(const SparseParams& p, const SparsePlan& pl, cudaStream_t st) 
     }
   }
   const unsigned nb = (unsigned)(p.B * p.units);
-  if (nb > 0) e = launch_dependent(sparse_merge_kernel<T, D, G>, dim3(nb), dim3(256), 0, st, p);
+  if (nb > 0) {
+    if (!p.n_peers && nb <= (unsigned)sm_count())
+      e = launch_dependent(sparse_merge_kernel<T, D, G, 1024>, dim3(nb), dim3(1024), 0, st, p);
+    else
+      e = launch_dependent(sparse_merge_kernel<T, D, G, 256>, dim3(nb), dim3(256), 0, st, p);
+  }
   if (e != cudaSuccess) return set_error(AKT_ERR_CUDA, std::string("sparse merge launch: ") + cudaGetErrorString(e));
   e = cudaGetLastError();
   if (e != cudaSuccess) return set_error(AKT_ERR_CUDA, std::string("sparse launch: ") + cudaGetErrorString(e));
@@ -924,7 +965,8 @@ int akt_sparse_dense_split_peer(const akt_sparse_dense_args* a, const akt_peer_e
     if (!x->peer_data[r] || !x->peer_flags[r]) return set_error(AKT_ERR_INVALID, "peer exchange: null peer pointer");
   if (!a || !a->out) return set_error(AKT_ERR_INVALID, "split_peer: output required");
   // the merge grid waits on itself: it must be resident at once (one CTA per
-  // (batch, unit), 256 threads; at least four fit on every SM)
+  // (batch, unit), 256 threads, at most 64 registers each: four fit on every
+  // SM; the launch also checks the occupancy the driver reports)
   if (a->num_kv_heads <= 0 || a->num_qo_heads % a->num_kv_heads) return set_error(AKT_ERR_INVALID, "heads");
   const int group = a->num_qo_heads / a->num_kv_heads;
   const int64_t units = (int64_t)a->batch * a->num_kv_heads * (group / sparse_group_tile(group, a->head_dim));
