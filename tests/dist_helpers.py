@@ -59,3 +59,28 @@ def oracle_paged_partial(buf, rows, D, q, shard, ind, nnz, K=None, L=None):
                 s = N.magicpig_logits(qf[b, h, 0], k, float(K[b, h]), float(L[b, h]), D)
             lse[b, h] = torch.logsumexp(s, 0)
             o[b, h] = torch.softmax(s, 0) @ v
+
+
+def init_group(backend, rank, world, port_q, device_id=None, timeout_s=60):
+    """Join a process group whose TCPStore rank 0 binds to a port the OS picks.
+
+    Rank 0 creates the store on port 0 (bound at once, so no other socket can
+    take it in between) and hands the port to the other ranks through
+    ``port_q``.  Picking a free port in the parent and binding it later in the
+    child races with every other socket on the machine, NCCL's own bootstrap
+    sockets included, and fails with "address already in use".
+    """
+    import datetime
+
+    import torch.distributed as dist
+    timeout = datetime.timedelta(seconds=timeout_s)
+    if rank == 0:
+        store = dist.TCPStore("127.0.0.1", 0, world, is_master=True, timeout=timeout, wait_for_workers=False)
+        for _ in range(world - 1):
+            port_q.put(store.port)
+    else:
+        store = dist.TCPStore("127.0.0.1", port_q.get(timeout=timeout_s * 2), world, is_master=False,
+                              timeout=timeout)
+    kw = {"device_id": device_id} if device_id is not None else {}
+    dist.init_process_group(backend, store=store, rank=rank, world_size=world, timeout=timeout, **kw)
+    return store

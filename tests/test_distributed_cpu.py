@@ -1,8 +1,6 @@
 """Host logic of the multi-GPU KV split on CPU: shard ranges, list sharding
 and rebasing, and the all-gather + merge orchestration across 2 gloo ranks
 (the CUDA partial/merge steps are replaced by CPU stand-ins here)."""
-import os
-import socket
 
 import pytest
 import torch
@@ -100,23 +98,14 @@ def test_paged_key_shard_tables_partition_the_pages(world):
         assert sorted(covered[b]) == list(range(16 * n))
 
 
-def _free_port():
-    s = socket.socket()
-    s.bind(("127.0.0.1", 0))
-    port = s.getsockname()[1]
-    s.close()
-    return port
 
-
-def _worker(rank, world, port, q):
+def _worker(rank, world, port_q, q):
     import torch.distributed as dist
 
     import dist_helpers as H
     from attention_kernel_triton_b200.distributed import sparsetoken_decode_kv_split
     from oracle import naive as N
-    os.environ["MASTER_ADDR"] = "127.0.0.1"
-    os.environ["MASTER_PORT"] = str(port)
-    dist.init_process_group("gloo", rank=rank, world_size=world)
+    H.init_group("gloo", rank, world, port_q)
     try:
         c = W.make_sparse_dense(B=1, Hq=8, Hkv=2, L=1000, D=64, keep_p=0.05, seed=3)
         lo, hi = shard_range(1000, world, rank)
@@ -133,8 +122,8 @@ def _worker(rank, world, port, q):
 def test_kv_split_orchestration_two_gloo_ranks(world):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    port_q = ctx.Queue()
+    procs = [ctx.Process(target=_worker, args=(r, world, port_q, q)) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
@@ -144,15 +133,13 @@ def test_kv_split_orchestration_two_gloo_ranks(world):
     assert max(errs.values()) <= 2e-3, errs
 
 
-def _paged_worker(rank, world, port, q, magic):
+def _paged_worker(rank, world, port_q, q, magic):
     import torch.distributed as dist
 
     import dist_helpers as H
     from attention_kernel_triton_b200.distributed import sparsetoken_decode_paged_kv_split
     from oracle import naive as N
-    os.environ["MASTER_ADDR"] = "127.0.0.1"
-    os.environ["MASTER_PORT"] = str(port)
-    dist.init_process_group("gloo", rank=rank, world_size=world)
+    H.init_group("gloo", rank, world, port_q)
     try:
         c = W.make_sparse_paged(B=2, Hq=8, Hkv=2, D=64, page_size=16, lens=[700, 333], keep_p=0.05, seed=5,
                                 magicpig=magic)
@@ -174,8 +161,8 @@ def _paged_worker(rank, world, port, q, magic):
 def test_paged_kv_split_orchestration_two_gloo_ranks(magic):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    port = _free_port()
-    procs = [ctx.Process(target=_paged_worker, args=(r, 2, port, q, magic)) for r in range(2)]
+    port_q = ctx.Queue()
+    procs = [ctx.Process(target=_paged_worker, args=(r, 2, port_q, q, magic)) for r in range(2)]
     for p in procs:
         p.start()
     for p in procs:

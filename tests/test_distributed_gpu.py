@@ -6,7 +6,6 @@ Tolerance: max-abs <= 2e-3 against the fp32 oracle, no NaNs.
 """
 import math
 import os
-import socket
 
 import pytest
 import torch
@@ -82,25 +81,15 @@ def test_lse_merge_matches_oracle_with_empty_parts():
     assert torch.all(out[5] == 0)
 
 
-def _free_port():
-    s = socket.socket()
-    s.bind(("127.0.0.1", 0))
-    port = s.getsockname()[1]
-    s.close()
-    return port
 
-
-def _nccl_worker(rank, world, port, q):
-    import datetime
-
+def _nccl_worker(rank, world, port_q, q):
     import torch.distributed as dist
-    os.environ["MASTER_ADDR"] = "127.0.0.1"
-    os.environ["MASTER_PORT"] = str(port)
+
+    import dist_helpers as H
     os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
     torch.cuda.set_device(rank)
     dev = torch.device("cuda", rank)
-    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
-                            timeout=datetime.timedelta(seconds=60))
+    H.init_group("nccl", rank, world, port_q, device_id=dev)
     try:
         c = W.make_sparse_dense(B=1, Hq=32, Hkv=8, L=32768, D=128, keep_p=0.02, seed=21)  # CPU, same on all ranks
         lo, hi = shard_range(32768, world, rank)
@@ -118,8 +107,8 @@ def _nccl_worker(rank, world, port, q):
 def test_kv_split_nccl_two_gpus():
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    port = _free_port()
-    procs = [ctx.Process(target=_nccl_worker, args=(r, 2, port, q)) for r in range(2)]
+    port_q = ctx.Queue()
+    procs = [ctx.Process(target=_nccl_worker, args=(r, 2, port_q, q)) for r in range(2)]
     for p in procs:
         p.start()
     for p in procs:
@@ -170,17 +159,14 @@ def test_peer_exchange_call_order_is_checked():
     assert _lib.device_status(0) == 0
 
 
-def _peer_worker(rank, world, port, q):
-    import datetime
-
+def _peer_worker(rank, world, port_q, q):
     import torch.distributed as dist
-    os.environ["MASTER_ADDR"] = "127.0.0.1"
-    os.environ["MASTER_PORT"] = str(port)
+
+    import dist_helpers as H
     os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
     torch.cuda.set_device(rank)
     dev = torch.device("cuda", rank)
-    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
-                            timeout=datetime.timedelta(seconds=60))
+    H.init_group("nccl", rank, world, port_q, device_id=dev)
     x = None
     try:
         c = W.make_sparse_dense(B=1, Hq=32, Hkv=8, L=32768, D=128, keep_p=0.02, seed=22)  # CPU, same on all ranks
@@ -208,8 +194,8 @@ def _peer_worker(rank, world, port, q):
 def test_peer_exchange_two_gpus():
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    port = _free_port()
-    procs = [ctx.Process(target=_peer_worker, args=(r, 2, port, q)) for r in range(2)]
+    port_q = ctx.Queue()
+    procs = [ctx.Process(target=_peer_worker, args=(r, 2, port_q, q)) for r in range(2)]
     for p in procs:
         p.start()
     for p in procs:
