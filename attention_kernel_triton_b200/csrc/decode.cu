@@ -434,8 +434,14 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
+// Paged calls below D=256 run four CTAs per SM (at most 102 registers, a 32 KB
+// stage ring each); the others three (64 KB rings; at D=256 the consumers
+// need more registers).  See the stage budget in make_plan.
+template <int D, bool PAGED>
+constexpr int mma_ctas_per_sm() { return (PAGED && D < 256) ? 4 : 3; }
+
 template <typename T, int D, int G, bool PAGED>
-__global__ void __launch_bounds__(kDecodeThreads, 3)
+__global__ void __launch_bounds__(kDecodeThreads, mma_ctas_per_sm<D, PAGED>())
     decode_mma_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
                       const DecodeParams p) {
   static_assert(D % 64 == 0 && D <= 256, "head_dim");
@@ -738,21 +744,23 @@ void layout_workspace(Plan& pl, bool paged, int B, int units, int D, int L, int 
 }
 
 // Tuning knobs, read once per thread: AKT_DECODE_STAGE_KB (shared-memory
-// budget of the K/V stage ring per CTA, default 64), AKT_DECODE_CHUNK_TILES
-// (upper bound on tiles per split-KV chunk, default 128; dense inputs count
-// 16 KB tiles, two of their 8 KB ones) and
-// AKT_DECODE_ITEMS_PER_SM (work items aimed at per SM, default 3: about one
-// wave at three CTAs per SM; large inputs hit the chunk bound instead).
+// budget of the K/V stage ring per CTA, default 64; 32 for paged tensor-core
+// calls below D=256), AKT_DECODE_CHUNK_TILES (upper bound on tiles per
+// split-KV chunk, default 128; dense inputs count 16 KB tiles, two of their
+// 8 KB ones) and AKT_DECODE_ITEMS_PER_SM (work items aimed at per SM, default
+// 3: about one wave at three CTAs per SM; large inputs hit the chunk bound
+// instead).
 int env_int(const char* name, int dflt) {
+  // the environment's value is cached (0: unset); the default is the call's
   static thread_local int cache[3] = {-1, -1, -1};
   const char k = name[11];
   int* slot = &cache[k == 'S' ? 0 : k == 'C' ? 1 : 2];
   if (*slot < 0) {
     const char* v = getenv(name);
     const int x = v ? atoi(v) : 0;
-    *slot = x > 0 ? x : dflt;
+    *slot = x > 0 ? x : 0;
   }
-  return *slot;
+  return *slot > 0 ? *slot : dflt;
 }
 
 // AKT_DECODE_TENSOR_CORES=0 selects the CUDA-core split-KV kernel for every
@@ -806,7 +814,12 @@ Plan make_plan(bool paged, int B, int Hq, int Hkv, int D, int L, int P, int64_t 
   // Consumer warp w takes tiles w, w+NW, ...; with NS a multiple of NW every
   // slot has one fixed consumer, so each mbarrier is waited phase by phase
   // (a parity wait is only unambiguous for the current or previous phase).
-  const size_t fit = (size_t)env_int("AKT_DECODE_STAGE_KB", 64) * 1024 / stage_bytes;
+  // Paged tensor-core calls below D=256: 32 KB rings (one stage per consumer
+  // warp) so that four CTAs fit per SM.  cfg3: kernel 764 -> 690 us (3 CTAs with
+  // 64 KB rings against 4 with 32 KB).  Dense calls keep 64 KB rings with three
+  // CTAs: at L=128K the 4-CTA form took 84.3 us against 81.1.
+  const bool four_per_sm = paged && pl.tc && D < 256;
+  const size_t fit = (size_t)env_int("AKT_DECODE_STAGE_KB", four_per_sm ? 32 : 64) * 1024 / stage_bytes;
   pl.num_stages = (int)std::max<size_t>(kConsumerWarps, std::min<size_t>(16, fit / kConsumerWarps * kConsumerWarps));
   // estimated tiles over all units -> chunk size: aim for about one wave of
   // CTAs (3 per SM), but no more than AKT_DECODE_CHUNK_TILES tiles per chunk
@@ -820,6 +833,8 @@ Plan make_plan(bool paged, int B, int Hq, int Hkv, int D, int L, int P, int64_t 
   // work items aimed at per SM: three (one wave at three CTAs per SM).  With
   // 8 KB dense stages this is also the best for dense inputs with many
   // (sequence, unit) pairs (8 x 1024 tokens at D=64: 16.9 us against 18.4 at two)
+  // (three also with four CTAs per SM: eight cfg3-like sequences took 90.9 us
+  // at four, 81.9 at three; 16 and 32 sequences and cfg3 the same either way)
   const int ips = env_int("AKT_DECODE_ITEMS_PER_SM", 3);
   const int64_t target = (int64_t)sm_count() * ips;
   int64_t ct = (total_tiles + target - 1) / target;

@@ -41,11 +41,11 @@ from attention_kernel_triton_b200 import workloads as W  # noqa: E402
 METRIC = "paged decode HBM GB/s"
 GRAPH_STEPS = 16  # e2e steps per captured CUDA graph
 # DRAM bytes of one split-KV launch on cfg3.  Tensor-core kernel: ncu on the
-# 8-sequence case (--batch 8: read 437.648 MB + write 3.849 MB for 437.439 MB of
+# 8-sequence case (--batch 8: read 437.694 MB + write 3.844 MB for 437.439 MB of
 # algorithmic bytes) scaled to cfg3's 4513.9 MB by the algorithmic bytes (reads
 # grow with the tokens; the partials' writes grow more slowly, so this bounds
 # them from above).  CUDA-core kernel: ncu on cfg3 itself (4.51 GB + 7.19 MB).
-CFG3_TRAFFIC_BYTES = (437.648e6 + 3.849e6) / 437.439e6 * 4513.900124e6
+CFG3_TRAFFIC_BYTES = (437.694e6 + 3.844e6) / 437.439e6 * 4513.900124e6
 CFG3_TRAFFIC_BYTES_CUDA_CORES = 4.51e9 + 7.19e6
 WORKLOAD = ("cfg3 paged var-len GQA decode: B=64 Hq=32 Hkv=8 D=128 fp16 page_size=16 "
             "lens U[512,32768] seeded, random physical page order")
