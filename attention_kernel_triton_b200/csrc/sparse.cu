@@ -446,7 +446,7 @@ __global__ void __launch_bounds__(kSThreads, MAGIC ? 3 : 4) sparse_decode_kernel
     const int kvh = unit / p.g_tiles;
     const int head0 = kvh * p.group + (unit - kvh * p.g_tiles) * G;
     const int p0 = c * kCP;
-    // round 1: nnz (CSR: row offsets), the page range (paged) and, for padded
+    // first load round: nnz (CSR: row offsets), the page range (paged) and, for padded
     // lists, the list entries themselves (positions < max_nnz exist; those
     // at or past nnz are masked once nnz is known)
     if (cta.tid < G) cta.nnz_s[cta.tid] = clamped_nnz(p, b, head0 + cta.tid);
@@ -464,7 +464,7 @@ __global__ void __launch_bounds__(kSThreads, MAGIC ? 3 : 4) sparse_decode_kernel
       }
     }
     __syncthreads();
-    // round 2: CSR entries (their row offset is checked by clamped_nnz, nnz 0
+    // second load round: CSR entries (their row offset is checked by clamped_nnz, nnz 0
     // if malformed); padded entries past nnz masked (each thread its own)
     for (int e = cta.tid; e < G * kCP; e += kSThreads) {
       const int h = e / kCP, j = e - h * kCP;
