@@ -300,3 +300,44 @@ def test_paged_decode_into_preallocated(cfg3):
     decode_paged_into(out, c.q, c.cache, c.indptr, c.indices, c.last_page_len)
     O = flash_attention_decode_paged(c.q, c.cache, c.indptr, c.indices, c.last_page_len)
     assert torch.equal(out, O)
+
+
+_CUDA_CORE_SCRIPT = r"""
+import sys, torch
+sys.path.insert(0, ".")
+sys.path.insert(0, "tests")
+from oracle import naive as N
+from attention_kernel_triton_b200 import _lib
+from attention_kernel_triton_b200 import workloads as W
+from attention_kernel_triton_b200.decode_flash_attention_redundant import flash_attention_decode
+from attention_kernel_triton_b200.decode_flash_attention_redundant_var_len_paged import flash_attention_decode_paged
+worst = 0.0
+for D, G, L in [(64, 4, 1000), (128, 4, 4096), (128, 1, 17)]:
+    c = W.make_decode(B=2, Hq=2 * G, Hkv=2, L=L, D=D, seed=D + G + L)
+    O = flash_attention_decode(c.q.cuda(), c.K.cuda(), c.V.cuda(), c.softmax_scale, c.group)
+    ref = N.decode_reference(c.q, c.K, c.V, c.softmax_scale, c.group)
+    worst = max(worst, float((O.float().cpu() - ref.float()).abs().max()))
+for D, G, P in [(128, 4, 16), (64, 2, 64)]:
+    c = W.make_paged(Hq=2 * G, Hkv=2, D=D, page_size=P, lens=[0, 1, 17, 300, 2000], seed=D + P)
+    O = flash_attention_decode_paged(c.q.cuda(), c.cache.cuda(), c.indptr.cuda(), c.indices.cuda(),
+                                     c.last_page_len.cuda())
+    ref = N.naive_paged_attention(c.q, c.cache, c.indptr, c.indices, c.last_page_len)
+    worst = max(worst, float((O.float().cpu() - ref.float()).abs().max()))
+torch.cuda.synchronize()
+print("max_err", worst, "status", _lib.device_status(0))
+sys.exit(0 if worst <= 2e-3 and _lib.device_status(0) == 0 else 1)
+"""
+
+
+def test_cuda_core_kernel_forced():
+    # Dense calls and paged calls with 16-key-multiple pages take the
+    # tensor-core kernel; AKT_DECODE_TENSOR_CORES=0 (read once per process)
+    # forces the CUDA-core kernel, which otherwise serves only other page
+    # sizes.  Run it in a child process against the oracle.
+    import subprocess
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    env = dict(os.environ, AKT_DECODE_TENSOR_CORES="0")
+    r = subprocess.run([sys.executable, "-c", _CUDA_CORE_SCRIPT], cwd=root, env=env, capture_output=True, text=True,
+                       timeout=600)
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
